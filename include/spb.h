@@ -1,0 +1,106 @@
+/*
+ * spb.h -- C ABI of the B200 sparse-FFN library (libspbatch_b200.so).
+ *
+ * Plain pointers, sizes and a cudaStream_t passed as void*; no C++ or torch
+ * types.  Every entry point is stream-ordered, performs no host
+ * synchronisation and returns an spb_status; spb_last_error() describes the
+ * last failure on the calling thread.  Scratch memory comes from a
+ * caller-owned device workspace whose size spb_ffn_workspace_bytes() reports.
+ *
+ * Each entry point names the reference interface it replaces
+ * (cuda/kernel.cuh / cuda/kernel.cu of SMAC-Zhang/SpBatch).  The reference's
+ * own C++ signatures are kept, unchanged, in include/spbatch/kernel.cuh and
+ * are implemented on top of these.
+ */
+#ifndef SPB_H_
+#define SPB_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+    SPB_OK = 0,
+    SPB_ERR_INVALID = 1,     /* bad shape, null pointer, unsupported combination */
+    SPB_ERR_WORKSPACE = 2,   /* workspace missing or too small */
+    SPB_ERR_CUDA = 3,        /* a CUDA runtime call failed */
+    SPB_ERR_UNSUPPORTED = 4, /* valid request this build cannot serve */
+} spb_status;
+
+/* Weight storage formats. */
+typedef enum {
+    SPB_W_F16 = 0,  /* fp16 rows of d values */
+    SPB_W_Q8_0 = 1, /* ggml Q8_0, split row layout (d int8 quants, then d/32 fp16 scales) */
+    SPB_W_Q4_0 = 2, /* ggml Q4_0, split row layout (d/2 nibble bytes, then d/32 fp16 scales) */
+} spb_wtype;
+
+/* Activation epilogues (cuda/kernel.cu:522-538). */
+typedef enum {
+    SPB_ACT_RELU_MUL = 0,      /* h = max(g,0) * u           (relu_and_mul_f32)  */
+    SPB_ACT_RELU_RELU_MUL = 1, /* h = max(g,0) * max(u,0)    (relu_relu_mul_f32) */
+} spb_act;
+
+/* Kernel path selection for spb_ffn_forward. */
+typedef enum {
+    SPB_PATH_AUTO = 0,   /* choose by batch size */
+    SPB_PATH_GEMV = 1,   /* CUDA-core gather GEMV (warp per neuron row) */
+    SPB_PATH_TENSOR = 2, /* tcgen05/TMEM gather GEMM */
+} spb_path;
+
+const char *spb_last_error(void);
+int spb_version(void);
+
+/*
+ * Device workspace needed by spb_union / spb_ffn_forward for a batch of B
+ * tokens, hidden size d, f neurons and union segments of `group` tokens
+ * (group = 0 means one segment holding the whole batch).
+ */
+size_t spb_ffn_workspace_bytes(int B, int d, int f, int group);
+
+/*
+ * Union and compaction of active neurons.
+ * Replaces get_idx_cuda (cuda/kernel.cuh:97, cuda/kernel.cu:877-937).
+ *   idx       [B][f] fp32 labels, neuron j active for token t iff idx > 0
+ *   group     tokens per segment: 8 = the reference's SPARSITY_GROUP_SIZE,
+ *             0 = whole batch as one segment; S = ceil(B / group) segments
+ *   merge_idx [S][f] out: ascending active neurons of each segment
+ *   act_cum   [S]    out: cumulative inclusive counts (act_neurons_device)
+ *   tok_bits  [B][ceil(f/32)] out (nullable): per-token activity bitmask
+ * Unlike the reference it accepts any B >= 1 and any f >= 1, and does not
+ * synchronise the stream.
+ */
+int spb_union(const float *idx, int B, int f, int group, int32_t *merge_idx, int32_t *act_cum,
+              uint32_t *tok_bits, void *workspace, size_t workspace_bytes, void *stream);
+
+/*
+ * One sparse FFN layer, out = W_down^T (act(W_gate x, W_up x) * mask).
+ * Replaces the MLP_BS composition (cuda/ffn_test.cu:129-142) of
+ * get_idx_cuda + gate_and_up_mul_mat_cuda_sparse + relu_and_mul_cuda +
+ * down_mul_mat_cuda_sparse (cuda/kernel.cu:877-1048) with a fused path.
+ *   w_gate, w_up [f][d], w_down stored [f][d] (the d x f matrix transposed,
+ *                as cuda/kernel.cu:726 reads it); format `wtype`
+ *   x    [B][d] fp32 (rounded to fp16 before the products, cuda/kernel.cu:978)
+ *   idx  [B][f] fp32 labels (> 0 active)
+ *   per_token_mask 1: h[t][j] = 0 unless neuron j is active for token t
+ *                     (the masked-dense FFN); 0: every neuron of the batch
+ *                     union contributes for every token (reference BS
+ *                     semantics with one segment)
+ *   out  [B][d] fp32, overwritten
+ *   merge_idx_out [f] (nullable): the batch union, ascending
+ *   count_out     [1] (nullable): its size U
+ * h is rounded to fp16 before the down projection (cuda/kernel.cu:1019);
+ * accumulation is fp32.
+ */
+int spb_ffn_forward(const void *w_gate, const void *w_up, const void *w_down, int wtype, const float *x,
+                    const float *idx, int B, int d, int f, int act, int per_token_mask, int path, float *out,
+                    int32_t *merge_idx_out, int32_t *count_out, void *workspace, size_t workspace_bytes,
+                    void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SPB_H_ */

@@ -1,0 +1,359 @@
+/*
+ * spb_oracle.c -- CPU restatement of the SpBatch activation-sparse FFN path.
+ *
+ * TEST INFRASTRUCTURE ONLY.  This file is the checker for the CUDA library in
+ * spbatch_b200/csrc; nothing in the product links or calls it.  Only tests/,
+ * __graft_entry__.smoke() and bench.py's CPU-baseline leg load it.
+ *
+ * Parity pins:
+ *   - spbo_union is checked bit-for-bit against the reference's own host
+ *     routine naive_sparsity_div (cuda/kernel.cu:1280-1297), compiled from the
+ *     reference sources into oracle/_ref by oracle/Makefile, and against the
+ *     committed fixtures in tests/golden generated from it.
+ *   - spbo_up_compact / spbo_down_compact restate naive_mm_up_kernel and
+ *     naive_mm_down_kernel (cuda/kernel.cu:1079-1113); the drop-in composition
+ *     restates MLP_naive (cuda/ffn_test.cu:144-163).  On a GPU box the tests
+ *     also run the reference's own naive kernels from oracle/_ref against them.
+ *   - Q4_0 / Q8_0 follow the ggml block formats named by the benchmark
+ *     definition (no ggml source is vendored in the reference: parity for the
+ *     quantised formats is unpinned beyond the half-block nibble placement of
+ *     cuda/kernel.cu:348,354-355).
+ *
+ * Accumulation is done in double so the oracle is closer to the exact value
+ * than either fp32 implementation; fp16 rounding points (x before gate/up,
+ * h before down; cuda/kernel.cu:946,978,1019) are reproduced exactly.
+ */
+#include <math.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+
+/* ---------------- IEEE binary16 conversion (round to nearest even) ------- */
+
+uint16_t spbo_f32_to_f16(float f) {
+    uint32_t x;
+    memcpy(&x, &f, 4);
+    uint32_t sign = (x >> 16) & 0x8000u;
+    uint32_t exp = (x >> 23) & 0xffu;
+    uint32_t man = x & 0x7fffffu;
+    if (exp == 0xffu) { /* inf / nan */
+        return (uint16_t)(sign | 0x7c00u | (man ? 0x200u : 0u));
+    }
+    int e = (int)exp - 127 + 15;
+    if (e >= 31) return (uint16_t)(sign | 0x7c00u); /* overflow -> inf */
+    if (e <= 0) {                                    /* subnormal or zero */
+        if (e < -10) return (uint16_t)sign;
+        man |= 0x800000u;
+        int shift = 14 - e; /* 24-bit mantissa -> (11 - 1 + e) bits */
+        uint32_t q = man >> shift;
+        uint32_t rem = man & ((1u << shift) - 1u);
+        uint32_t half = 1u << (shift - 1);
+        if (rem > half || (rem == half && (q & 1u))) q++;
+        return (uint16_t)(sign | q);
+    }
+    uint32_t q = ((uint32_t)e << 10) | (man >> 13);
+    uint32_t rem = man & 0x1fffu;
+    if (rem > 0x1000u || (rem == 0x1000u && (q & 1u))) q++; /* may carry into exp: fine */
+    return (uint16_t)(sign | q);
+}
+
+float spbo_f16_to_f32(uint16_t h) {
+    uint32_t sign = ((uint32_t)h & 0x8000u) << 16;
+    uint32_t exp = (h >> 10) & 0x1fu;
+    uint32_t man = h & 0x3ffu;
+    uint32_t x;
+    if (exp == 0) {
+        if (man == 0) {
+            x = sign;
+        } else { /* subnormal: normalise */
+            int e = -1;
+            do { man <<= 1; e++; } while (!(man & 0x400u));
+            man &= 0x3ffu;
+            x = sign | ((uint32_t)(127 - 15 - e) << 23) | (man << 13);
+        }
+    } else if (exp == 31) {
+        x = sign | 0x7f800000u | (man << 13);
+    } else {
+        x = sign | ((exp - 15 + 127) << 23) | (man << 13);
+    }
+    float f;
+    memcpy(&f, &x, 4);
+    return f;
+}
+
+static inline float r16(float v) { return spbo_f16_to_f32(spbo_f32_to_f16(v)); }
+
+void spbo_round_f16(const float *in, float *out, int64_t n) {
+    for (int64_t i = 0; i < n; ++i) out[i] = r16(in[i]);
+}
+
+void spbo_f32_to_f16_array(const float *in, uint16_t *out, int64_t n) {
+    for (int64_t i = 0; i < n; ++i) out[i] = spbo_f32_to_f16(in[i]);
+}
+
+/* ---------------- union / compaction ------------------------------------- */
+
+/*
+ * Segment union of active neurons, ascending.  A neuron is active for a token
+ * when idx[t*f + j] > 0 (cuda/kernel.cu:553, 1289).  Tokens are split into
+ * consecutive segments of G tokens (G = 8 is the reference's
+ * SPARSITY_GROUP_SIZE; G = B gives the whole-batch union; a short last segment
+ * is allowed when B % G != 0).  merge_idx[s*f + c] holds the c-th active
+ * neuron of segment s; counts[s] is the per-segment count exactly as
+ * naive_sparsity_div returns it (cuda/kernel.cu:1280-1297).
+ */
+void spbo_union(const float *idx, int B, int f, int G, int32_t *merge_idx, int32_t *counts) {
+    int S = (B + G - 1) / G;
+    for (int s = 0; s < S; ++s) {
+        int t0 = s * G, t1 = t0 + G < B ? t0 + G : B;
+        int cnt = 0;
+        for (int j = 0; j < f; ++j) {
+            int any = 0;
+            for (int t = t0; t < t1; ++t) any |= (idx[(int64_t)t * f + j] > 0.0f);
+            if (any) merge_idx[(int64_t)s * f + cnt++] = j;
+        }
+        counts[s] = cnt;
+    }
+}
+
+/* Per-token activity bitmask: bit (j % 32) of word bits[t*W + j/32]. */
+void spbo_token_bits(const float *idx, int B, int f, uint32_t *bits) {
+    int W = (f + 31) / 32;
+    memset(bits, 0, sizeof(uint32_t) * (size_t)B * W);
+    for (int t = 0; t < B; ++t)
+        for (int j = 0; j < f; ++j)
+            if (idx[(int64_t)t * f + j] > 0.0f) bits[(int64_t)t * W + j / 32] |= 1u << (j % 32);
+}
+
+/* ---------------- compacted gather GEMMs (drop-in semantics) ------------- */
+
+/*
+ * naive_mm_up_kernel restated (cuda/kernel.cu:1079-1095): for token t in
+ * segment s and compacted slot r < counts[s],
+ *   dst[t*f + r] = sum_k W[merge_idx[s*f + r]][k] * x[t][k]
+ * W is [f][d] fp16 (bit patterns), x is [B][d] fp32.  round_x = 1 rounds x to
+ * fp16 first, as up_mul_mat_cuda_sparse does (cuda/kernel.cu:946, 978).
+ * Slots r >= counts[s] are left untouched.
+ */
+void spbo_up_compact(const uint16_t *w, const float *x, const int32_t *merge_idx, const int32_t *counts,
+                     int B, int d, int f, int G, int round_x, float *dst) {
+    float *xr = (float *)malloc(sizeof(float) * d);
+    for (int t = 0; t < B; ++t) {
+        int s = t / G;
+        for (int k = 0; k < d; ++k) {
+            float v = x[(int64_t)t * d + k];
+            xr[k] = round_x ? r16(v) : v;
+        }
+        for (int r = 0; r < counts[s]; ++r) {
+            const uint16_t *row = w + (int64_t)merge_idx[(int64_t)s * f + r] * d;
+            double acc = 0.0;
+            for (int k = 0; k < d; ++k) acc += (double)spbo_f16_to_f32(row[k]) * (double)xr[k];
+            dst[(int64_t)t * f + r] = (float)acc;
+        }
+    }
+    free(xr);
+}
+
+/*
+ * naive_mm_down_kernel restated (cuda/kernel.cu:1097-1113): W_down is stored
+ * [f][d] (the d x f matrix transposed), h is compacted [B][f] fp32,
+ *   dst[t*d + m] = sum_{r < counts[s]} Wd[merge_idx[s*f + r]][m] * h[t][r]
+ * round_h = 1 rounds h to fp16 first (cuda/kernel.cu:1019).
+ */
+void spbo_down_compact(const uint16_t *wd, const float *h, const int32_t *merge_idx, const int32_t *counts,
+                       int B, int d, int f, int G, int round_h, float *dst) {
+    double *acc = (double *)malloc(sizeof(double) * d);
+    for (int t = 0; t < B; ++t) {
+        int s = t / G;
+        for (int m = 0; m < d; ++m) acc[m] = 0.0;
+        for (int r = 0; r < counts[s]; ++r) {
+            float hv = h[(int64_t)t * f + r];
+            if (round_h) hv = r16(hv);
+            if (hv == 0.0f) continue;
+            const uint16_t *row = wd + (int64_t)merge_idx[(int64_t)s * f + r] * d;
+            for (int m = 0; m < d; ++m) acc[m] += (double)spbo_f16_to_f32(row[m]) * (double)hv;
+        }
+        for (int m = 0; m < d; ++m) dst[(int64_t)t * d + m] = (float)acc[m];
+    }
+    free(acc);
+}
+
+/* ---------------- full sparse FFN ----------------------------------------- */
+
+/*
+ * Sparse FFN forward for one layer.
+ *   mode 0 (segment union, reference BS semantics, cuda/ffn_test.cu:129-163):
+ *          every neuron in the token's segment union contributes.
+ *   mode 1 (per-token mask, the masked-dense FFN): only neurons with
+ *          idx[t][j] > 0 contribute.
+ *   act 0: h = max(g,0) * u         (relu_and_mul_f32, cuda/kernel.cu:522-529)
+ *   act 1: h = max(g,0) * max(u,0)  (relu_relu_mul_f32, cuda/kernel.cu:531-538)
+ * x is rounded to fp16 before gate/up; h is rounded to fp16 before down.
+ * out is [B][d] fp32.
+ */
+void spbo_ffn(const uint16_t *wg, const uint16_t *wu, const uint16_t *wd, const float *x, const float *idx,
+              int B, int d, int f, int G, int mode, int act, float *out) {
+    int S = (B + G - 1) / G;
+    int32_t *merge = (int32_t *)malloc(sizeof(int32_t) * (size_t)S * f);
+    int32_t *counts = (int32_t *)malloc(sizeof(int32_t) * S);
+    spbo_union(idx, B, f, G, merge, counts);
+    float *xr = (float *)malloc(sizeof(float) * d);
+    double *acc = (double *)malloc(sizeof(double) * d);
+    for (int t = 0; t < B; ++t) {
+        int s = t / G;
+        for (int k = 0; k < d; ++k) xr[k] = r16(x[(int64_t)t * d + k]);
+        for (int m = 0; m < d; ++m) acc[m] = 0.0;
+        for (int r = 0; r < counts[s]; ++r) {
+            int j = merge[(int64_t)s * f + r];
+            if (mode == 1 && !(idx[(int64_t)t * f + j] > 0.0f)) continue;
+            const uint16_t *rg = wg + (int64_t)j * d;
+            const uint16_t *ru = wu + (int64_t)j * d;
+            double g = 0.0, u = 0.0;
+            for (int k = 0; k < d; ++k) {
+                g += (double)spbo_f16_to_f32(rg[k]) * (double)xr[k];
+                u += (double)spbo_f16_to_f32(ru[k]) * (double)xr[k];
+            }
+            float gf = (float)g, uf = (float)u;
+            float hf = (gf > 0.0f ? gf : 0.0f) * (act == 1 ? (uf > 0.0f ? uf : 0.0f) : uf);
+            hf = r16(hf);
+            if (hf == 0.0f) continue;
+            const uint16_t *rd = wd + (int64_t)j * d;
+            for (int m = 0; m < d; ++m) acc[m] += (double)spbo_f16_to_f32(rd[m]) * (double)hf;
+        }
+        for (int m = 0; m < d; ++m) out[(int64_t)t * d + m] = (float)acc[m];
+    }
+    free(acc);
+    free(xr);
+    free(counts);
+    free(merge);
+}
+
+/* ---------------- ggml block quantisation --------------------------------- */
+
+/*
+ * Q8_0: blocks of 32 along each row; scale d = absmax / 127 stored as fp16;
+ * q = round(x / d) as int8.  Dequantised value = q * fp16(d).
+ * Q4_0: blocks of 32; with m = the element of largest magnitude (sign kept),
+ * d = m / -8 stored as fp16, q = min(15, (int)(x / d + 8.5)) in [0, 15];
+ * byte j of the block holds element j in its low nibble and element j + 16 in
+ * its high nibble (the half-block placement of cuda/kernel.cu:348,354-355).
+ * Dequantised value = (q - 8) * fp16(d).
+ *
+ * Output layout per row (n = row length, a multiple of 32): the quant bytes of
+ * all blocks first (n bytes for Q8_0, n/2 for Q4_0), then the n/32 fp16 scales.
+ * This is the "split" row layout the GPU kernels read.
+ */
+void spbo_quantize_q8_0(const float *w, int rows, int n, uint8_t *out) {
+    int nb = n / 32;
+    int64_t row_bytes = (int64_t)n + 2 * nb;
+    for (int r = 0; r < rows; ++r) {
+        const float *x = w + (int64_t)r * n;
+        int8_t *qs = (int8_t *)(out + r * row_bytes);
+        uint16_t *sc = (uint16_t *)(out + r * row_bytes + n);
+        for (int b = 0; b < nb; ++b) {
+            float amax = 0.0f;
+            for (int i = 0; i < 32; ++i) {
+                float a = fabsf(x[b * 32 + i]);
+                if (a > amax) amax = a;
+            }
+            float dd = amax / 127.0f;
+            float id = dd != 0.0f ? 1.0f / dd : 0.0f;
+            for (int i = 0; i < 32; ++i) qs[b * 32 + i] = (int8_t)roundf(x[b * 32 + i] * id);
+            uint16_t hs = spbo_f32_to_f16(dd);
+            memcpy(&sc[b], &hs, 2);
+        }
+    }
+}
+
+void spbo_quantize_q4_0(const float *w, int rows, int n, uint8_t *out) {
+    int nb = n / 32;
+    int64_t row_bytes = (int64_t)n / 2 + 2 * nb;
+    for (int r = 0; r < rows; ++r) {
+        const float *x = w + (int64_t)r * n;
+        uint8_t *qs = out + r * row_bytes;
+        uint16_t *sc = (uint16_t *)(out + r * row_bytes + n / 2);
+        for (int b = 0; b < nb; ++b) {
+            float amax = 0.0f, m = 0.0f;
+            for (int i = 0; i < 32; ++i) {
+                float v = x[b * 32 + i];
+                if (fabsf(v) > amax) { amax = fabsf(v); m = v; }
+            }
+            float dd = m / -8.0f;
+            float id = dd != 0.0f ? 1.0f / dd : 0.0f;
+            for (int j = 0; j < 16; ++j) {
+                int q0 = (int)(x[b * 32 + j] * id + 8.5f);
+                int q1 = (int)(x[b * 32 + j + 16] * id + 8.5f);
+                if (q0 > 15) q0 = 15;
+                if (q1 > 15) q1 = 15;
+                qs[b * 16 + j] = (uint8_t)(q0 | (q1 << 4));
+            }
+            uint16_t hs = spbo_f32_to_f16(dd);
+            memcpy(&sc[b], &hs, 2);
+        }
+    }
+}
+
+/* Dequantise quantised rows (split layout above) to fp32; qtype 8 or 4. */
+void spbo_dequantize(const uint8_t *q, int qtype, int rows, int n, float *out) {
+    int nb = n / 32;
+    int64_t qbytes = qtype == 8 ? n : n / 2;
+    int64_t row_bytes = qbytes + 2 * nb;
+    for (int r = 0; r < rows; ++r) {
+        const uint8_t *qs = q + r * row_bytes;
+        const uint16_t *sc = (const uint16_t *)(q + r * row_bytes + qbytes);
+        float *y = out + (int64_t)r * n;
+        for (int b = 0; b < nb; ++b) {
+            uint16_t hs;
+            memcpy(&hs, &sc[b], 2);
+            float dd = spbo_f16_to_f32(hs);
+            if (qtype == 8) {
+                for (int i = 0; i < 32; ++i) y[b * 32 + i] = (float)((const int8_t *)qs)[b * 32 + i] * dd;
+            } else {
+                for (int j = 0; j < 16; ++j) {
+                    uint8_t v = qs[b * 16 + j];
+                    y[b * 32 + j] = (float)((int)(v & 0xf) - 8) * dd;
+                    y[b * 32 + j + 16] = (float)((int)(v >> 4) - 8) * dd;
+                }
+            }
+        }
+    }
+}
+
+/*
+ * Sparse FFN with fp32 (already dequantised) weights: same contract as
+ * spbo_ffn but the weights are fp32 arrays.  Used for the Q4_0/Q8_0 paths,
+ * whose dequantised values are exactly representable in fp32.
+ */
+void spbo_ffn_f32w(const float *wg, const float *wu, const float *wd, const float *x, const float *idx,
+                   int B, int d, int f, int G, int mode, int act, float *out) {
+    int S = (B + G - 1) / G;
+    int32_t *merge = (int32_t *)malloc(sizeof(int32_t) * (size_t)S * f);
+    int32_t *counts = (int32_t *)malloc(sizeof(int32_t) * S);
+    spbo_union(idx, B, f, G, merge, counts);
+    float *xr = (float *)malloc(sizeof(float) * d);
+    double *acc = (double *)malloc(sizeof(double) * d);
+    for (int t = 0; t < B; ++t) {
+        int s = t / G;
+        for (int k = 0; k < d; ++k) xr[k] = r16(x[(int64_t)t * d + k]);
+        for (int m = 0; m < d; ++m) acc[m] = 0.0;
+        for (int r = 0; r < counts[s]; ++r) {
+            int j = merge[(int64_t)s * f + r];
+            if (mode == 1 && !(idx[(int64_t)t * f + j] > 0.0f)) continue;
+            double g = 0.0, u = 0.0;
+            for (int k = 0; k < d; ++k) {
+                g += (double)wg[(int64_t)j * d + k] * (double)xr[k];
+                u += (double)wu[(int64_t)j * d + k] * (double)xr[k];
+            }
+            float gf = (float)g, uf = (float)u;
+            float hf = (gf > 0.0f ? gf : 0.0f) * (act == 1 ? (uf > 0.0f ? uf : 0.0f) : uf);
+            hf = r16(hf);
+            if (hf == 0.0f) continue;
+            for (int m = 0; m < d; ++m) acc[m] += (double)wd[(int64_t)j * d + m] * (double)hf;
+        }
+        for (int m = 0; m < d; ++m) out[(int64_t)t * d + m] = (float)acc[m];
+    }
+    free(acc);
+    free(xr);
+    free(counts);
+    free(merge);
+}

@@ -1,0 +1,158 @@
+"""spbatch_b200 -- B200-native activation-sparse FFN (SpBatch hot path).
+
+Python host bindings over ``libspbatch_b200.so`` (C ABI in ``include/spb.h``;
+the reference's C++ API in ``include/spbatch/kernel.cuh``).  PyTorch supplies
+device memory and streams only; every computation runs in the library's CUDA
+kernels.  There is no CPU fallback: importing the bindings without the built
+library raises, and calling them without a GPU raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+from . import workload  # noqa: F401
+
+PKG = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(PKG, "libspbatch_b200.so")
+
+SPB_OK = 0
+W_F16, W_Q8_0, W_Q4_0 = 0, 1, 2
+ACT_RELU_MUL, ACT_RELU_RELU_MUL = 0, 1
+PATH_AUTO, PATH_GEMV, PATH_TENSOR = 0, 1, 2
+
+_lib = None
+
+
+class SpbError(RuntimeError):
+    pass
+
+
+def lib() -> C.CDLL:
+    """Loads libspbatch_b200.so (build it with ``python -m spbatch_b200.build``)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise SpbError(f"{LIB_PATH} is missing: run `python -m spbatch_b200.build`")
+        L = C.CDLL(LIB_PATH)
+        P, I, Z = C.c_void_p, C.c_int, C.c_size_t
+        L.spb_last_error.restype = C.c_char_p
+        L.spb_version.restype = I
+        L.spb_ffn_workspace_bytes.argtypes = [I, I, I, I]
+        L.spb_ffn_workspace_bytes.restype = Z
+        L.spb_union.argtypes = [P, I, I, I, P, P, P, P, Z, P]
+        L.spb_ffn_forward.argtypes = [P, P, P, I, P, P, I, I, I, I, I, I, P, P, P, P, Z, P]
+        _lib = L
+    return _lib
+
+
+def _check(rc: int, what: str) -> None:
+    if rc != SPB_OK:
+        raise SpbError(f"{what} failed ({rc}): {lib().spb_last_error().decode()}")
+
+
+def _ptr(t) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _stream(stream=None) -> int:
+    import torch
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return s.cuda_stream
+
+
+def _require_cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise SpbError("spbatch_b200 operates on CUDA tensors only (no CPU fallback)")
+        if t is not None and not t.is_contiguous():
+            raise SpbError("spbatch_b200 needs contiguous tensors")
+
+
+def workspace_bytes(B: int, d: int, f: int, group: int = 0) -> int:
+    return int(lib().spb_ffn_workspace_bytes(B, d, f, group))
+
+
+def new_workspace(B: int, d: int, f: int, group: int = 0, device=None):
+    import torch
+    return torch.empty(workspace_bytes(B, d, f, group), dtype=torch.uint8, device=device or "cuda")
+
+
+def union(idx, group: int = 0, workspace=None, stream=None):
+    """Segment union of active neurons (replaces get_idx_cuda).
+
+    Returns (merge_idx [S][f] int32, act_cum [S] int32 cumulative, tok_bits
+    [B][ceil(f/32)] int32 bit words).  group=0: one segment for the batch.
+    """
+    import torch
+    _require_cuda(idx)
+    B, f = idx.shape
+    G = B if group == 0 else group
+    S = (B + G - 1) // G
+    dev = idx.device
+    merge = torch.zeros((S, f), dtype=torch.int32, device=dev)
+    act = torch.zeros(S, dtype=torch.int32, device=dev)
+    bits = torch.zeros((B, (f + 31) // 32), dtype=torch.int32, device=dev)
+    ws = workspace if workspace is not None else new_workspace(B, 64, f, group, dev)
+    _check(lib().spb_union(idx.data_ptr(), B, f, group, merge.data_ptr(), act.data_ptr(), bits.data_ptr(),
+                           ws.data_ptr(), ws.numel(), _stream(stream)), "spb_union")
+    return merge, act, bits
+
+
+def ffn_forward(w_gate, w_up, w_down, x, idx, *, wtype: int = W_F16, act: int = ACT_RELU_MUL,
+                per_token_mask: bool = True, path: int = PATH_AUTO, out=None, workspace=None,
+                merge_idx_out=None, count_out=None, stream=None):
+    """One sparse FFN layer on the GPU (see spb_ffn_forward in include/spb.h).
+
+    w_gate / w_up / w_down: [f][d] rows (W_down stored transposed, as the
+    reference stores it); x [B][d] fp32; idx [B][f] fp32 labels (> 0 active).
+    """
+    import torch
+    _require_cuda(w_gate, w_up, w_down, x, idx, out, merge_idx_out, count_out)
+    B, d = x.shape
+    f = idx.shape[1]
+    if out is None:
+        out = torch.empty((B, d), dtype=torch.float32, device=x.device)
+    ws = workspace if workspace is not None else new_workspace(B, d, f, 0, x.device)
+    _check(lib().spb_ffn_forward(w_gate.data_ptr(), w_up.data_ptr(), w_down.data_ptr(), wtype, x.data_ptr(),
+                                 idx.data_ptr(), B, d, f, act, int(per_token_mask), path, out.data_ptr(),
+                                 _ptr(merge_idx_out), _ptr(count_out), ws.data_ptr(), ws.numel(),
+                                 _stream(stream)), "spb_ffn_forward")
+    return out
+
+
+class dropin:
+    """The reference's C++ API (include/spbatch/kernel.cuh), bound by its
+    mangled names, with the reference's argument order and M/N/K meanings."""
+
+    _SYMS = {
+        "get_idx_cuda": ("_Z12get_idx_cudaPKfPiS1_iiP11CUstream_st", "PPPiiP"),
+        "up_mul_mat_cuda_sparse": ("_Z22up_mul_mat_cuda_sparsePK6__halfPKfPfPiiiiPKiP11CUstream_st", "PPPPiiiPP"),
+        "gate_and_up_mul_mat_cuda_sparse": (
+            "_Z31gate_and_up_mul_mat_cuda_sparsePK6__halfS1_PKfPfS4_PiiiiPKiP11CUstream_stS9_", "PPPPPPiiiPPP"),
+        "relu_and_mul_cuda": ("_Z17relu_and_mul_cudaPKfS0_PfiiP11CUstream_st", "PPPiiP"),
+        "relu_relu_mul_cuda": ("_Z18relu_relu_mul_cudaPKfS0_PfiiP11CUstream_st", "PPPiiP"),
+        "down_mul_mat_cuda_sparse": ("_Z24down_mul_mat_cuda_sparsePK6__halfPKfPfPiiiiPKiP11CUstream_st",
+                                     "PPPPiiiPP"),
+        "naive_mm_up_cuda": ("_Z16naive_mm_up_cudaPK6__halfPKfPfiiiPKiPiP11CUstream_st", "PPPiiiPPP"),
+        "naive_mm_down_cuda": ("_Z18naive_mm_down_cudaPK6__halfPKfPfiiiPKiPiP11CUstream_st", "PPPiiiPPP"),
+        "naive_sparsity_div": ("_Z18naive_sparsity_divPKfPiS1_ii", "PPPii"),
+        "convert_fp32_to_fp16_cuda": ("_Z25convert_fp32_to_fp16_cudaPKvP6__halfiP11CUstream_st", "PPiP"),
+        "convert_fp16_to_fp32_cuda": ("_Z25convert_fp16_to_fp32_cudaPKvPfiP11CUstream_st", "PPiP"),
+        "convert_mul_mat_batch_f16_cuda_sparse": (
+            "_Z37convert_mul_mat_batch_f16_cuda_sparsePKvPKfPfiiiiP11CUstream_stPiS3_", "PPPiiiiPPP"),
+        "convert_axpy_sparse_batch_f16_cuda": (
+            "_Z34convert_axpy_sparse_batch_f16_cudaPKvPKfPfiiiiP11CUstream_stPiS3_", "PPPiiiiPPP"),
+        "relu_f32_cuda": ("_Z13relu_f32_cudaPKfPfiP11CUstream_st", "PPiP"),
+        "mul_f32_cuda": ("_Z12mul_f32_cudaPKfS0_PfiiP11CUstream_st", "PPPiiP"),
+        "add_sparse_cuda": ("_Z15add_sparse_cudaPKfPK6__halfPfiiPKiS6_P11CUstream_st", "PPPiiPPP"),
+        "gemm_cuda": ("_Z9gemm_cudaPK6__halfPKfPfiiiP11CUstream_st", "PPPiiiP"),
+    }
+
+    @classmethod
+    def fn(cls, name: str, library=None):
+        sym, sig = cls._SYMS[name]
+        f = getattr(library or lib(), sym)
+        f.argtypes = [C.c_void_p if c == "P" else C.c_int for c in sig]
+        f.restype = None
+        return f

@@ -1,0 +1,135 @@
+// C ABI (include/spb.h): argument checking, workspace carving and launch
+// sequencing.  No entry point synchronises the host or allocates memory.
+#include <cstdio>
+#include <mutex>
+#include <vector>
+
+#include "spb_internal.h"
+
+namespace spb {
+
+static thread_local std::string g_last_error;
+
+void set_error(const std::string &msg) { g_last_error = msg; }
+
+int fail(int status, const std::string &msg) {
+    g_last_error = msg;
+    return status;
+}
+
+int cuda_fail(cudaError_t e, const char *what) {
+    g_last_error = std::string(what) + ": " + cudaGetErrorName(e) + " (" + cudaGetErrorString(e) + ")";
+    return SPB_ERR_CUDA;
+}
+
+int num_sms() {
+    static std::mutex mu;
+    static std::vector<int> cache;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return kNumSMs;
+    std::lock_guard<std::mutex> lk(mu);
+    if ((int)cache.size() <= dev) cache.resize(dev + 1, 0);
+    if (cache[dev] == 0) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = kNumSMs;
+        cache[dev] = n;
+    }
+    return cache[dev];
+}
+
+int ensure_smem(const void *kernel, size_t bytes) {
+    static std::mutex mu;
+    static std::vector<std::pair<std::pair<int, const void *>, size_t>> done;
+    int dev = 0;
+    SPB_CUDA_TRY(cudaGetDevice(&dev));
+    std::lock_guard<std::mutex> lk(mu);
+    for (auto &e : done) {
+        if (e.first.first == dev && e.first.second == kernel) {
+            if (e.second >= bytes) return SPB_OK;
+            SPB_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
+            e.second = bytes;
+            return SPB_OK;
+        }
+    }
+    if (bytes > 48 * 1024)
+        SPB_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
+    done.push_back({{dev, kernel}, bytes < 48 * 1024 ? 48 * 1024 : bytes});
+    return SPB_OK;
+}
+
+static bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace spb
+
+using namespace spb;
+
+extern "C" {
+
+const char *spb_last_error(void) { return g_last_error.c_str(); }
+
+int spb_version(void) { return 1; }
+
+size_t spb_ffn_workspace_bytes(int B, int d, int f, int group) {
+    if (B <= 0 || d <= 0 || f <= 0) return 0;
+    return carve_workspace(nullptr, B, d, f, group).bytes;
+}
+
+int spb_union(const float *idx, int B, int f, int group, int32_t *merge_idx, int32_t *act_cum, uint32_t *tok_bits,
+              void *workspace, size_t workspace_bytes, void *stream) {
+    if (!idx || !merge_idx || !act_cum) return fail(SPB_ERR_INVALID, "spb_union: null pointer");
+    if (B <= 0 || f <= 0 || group < 0) return fail(SPB_ERR_INVALID, "spb_union: bad shape");
+    const int G = group == 0 ? B : group;
+    const int S = (B + G - 1) / G;
+    Workspace ws = carve_workspace(workspace, B, 0, f, group);
+    if (!workspace || workspace_bytes < ws.bytes) return fail(SPB_ERR_WORKSPACE, "spb_union: workspace too small");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    int rc = launch_union_bits(idx, B, f, G, tok_bits, ws.seg_bits, nullptr, 0, st);
+    if (rc) return rc;
+    return launch_compact(ws.seg_bits, S, f, merge_idx, act_cum, ws.counts, st);
+}
+
+int spb_ffn_forward(const void *w_gate, const void *w_up, const void *w_down, int wtype, const float *x,
+                    const float *idx, int B, int d, int f, int act, int per_token_mask, int path, float *out,
+                    int32_t *merge_idx_out, int32_t *count_out, void *workspace, size_t workspace_bytes,
+                    void *stream) {
+    if (!w_gate || !w_up || !w_down || !x || !idx || !out) return fail(SPB_ERR_INVALID, "spb_ffn_forward: null pointer");
+    if (B <= 0 || d <= 0 || f <= 0) return fail(SPB_ERR_INVALID, "spb_ffn_forward: bad shape");
+    if (d % 64 != 0) return fail(SPB_ERR_INVALID, "spb_ffn_forward: d must be a multiple of 64");
+    if (wtype != SPB_W_F16 && wtype != SPB_W_Q8_0 && wtype != SPB_W_Q4_0)
+        return fail(SPB_ERR_INVALID, "spb_ffn_forward: unknown weight type");
+    if (act != SPB_ACT_RELU_MUL && act != SPB_ACT_RELU_RELU_MUL)
+        return fail(SPB_ERR_INVALID, "spb_ffn_forward: unknown activation");
+    if (!aligned16(w_gate) || !aligned16(w_up) || !aligned16(w_down) || !aligned16(x) || !aligned16(out))
+        return fail(SPB_ERR_INVALID, "spb_ffn_forward: weights, x and out must be 16-byte aligned");
+    if (words_of(f) > 1024) return fail(SPB_ERR_UNSUPPORTED, "spb_ffn_forward: f > 32768");
+    Workspace ws = carve_workspace(workspace, B, d, f, 0);
+    if (!workspace || workspace_bytes < ws.bytes)
+        return fail(SPB_ERR_WORKSPACE, "spb_ffn_forward: workspace too small");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+
+    if (path == SPB_PATH_AUTO) path = SPB_PATH_GEMV;
+    if (path != SPB_PATH_GEMV) return fail(SPB_ERR_UNSUPPORTED, "spb_ffn_forward: tensor path not built yet");
+
+    int rc = launch_union_bits(idx, B, f, B, ws.tok_bits, ws.seg_bits, out, (int64_t)B * d, st);
+    if (rc) return rc;
+    FusedGemvArgs a{};
+    a.wg = w_gate;
+    a.wu = w_up;
+    a.wd = w_down;
+    a.wtype = wtype;
+    a.x = x;
+    a.B = B;
+    a.d = d;
+    a.f = f;
+    a.seg_bits = ws.seg_bits;
+    a.tok_bits = ws.tok_bits;
+    a.act = act;
+    a.per_token = per_token_mask;
+    a.h = ws.h;
+    a.merge = merge_idx_out ? merge_idx_out : ws.merge_idx;
+    a.count = count_out ? count_out : ws.counts;
+    a.out = out;
+    return launch_fused_gemv(a, st);
+}
+
+}  // extern "C"

@@ -1,0 +1,133 @@
+// Union / compaction of per-token active-neuron sets.
+//
+// Replaces the reference's four-launch get_idx_cuda sequence
+// (merge_batch_sparsity_kernel -> cub::DeviceScan::InclusiveSum ->
+// move_activation -> generate_indices_kernel + cudaStreamSynchronize,
+// cuda/kernel.cu:540-593, 877-937) with two launches and no host sync:
+//
+//   union_bits_kernel  one warp per 32-neuron word: ballot over every token's
+//                      label (coalesced 128-byte loads), writes per-token and
+//                      per-segment bit words; also zero-fills the FFN output
+//                      the down projection accumulates into.
+//   compact_kernel     one CTA per segment: block scan of word popcounts and
+//                      ascending emission of neuron ids, plus the cumulative
+//                      counts the reference's act_neurons_device holds.
+//
+// The fused FFN path skips compact_kernel: its CTAs rebuild the slice of the
+// index list they own from the segment bits (spb_scan.cuh).
+#include "spb_internal.h"
+#include "spb_scan.cuh"
+
+namespace spb {
+
+constexpr int kUnionWarps = 8;
+
+__global__ void __launch_bounds__(kUnionWarps * 32)
+union_bits_kernel(const float *__restrict__ idx, int B, int f, int W, int G, uint32_t *__restrict__ tok_bits,
+                  uint32_t *__restrict__ seg_bits, float *__restrict__ zero_out, int64_t zero_n) {
+    const int lane = threadIdx.x & 31;
+    const int w = blockIdx.x * kUnionWarps + (threadIdx.x >> 5);
+    if (w < W) {
+        const int j = w * 32 + lane;
+        const bool in = j < f;
+        uint32_t seg = 0;
+        int t = 0;
+        constexpr int U = 8;
+        for (; t + U <= B; t += U) {
+            float v[U];
+#pragma unroll
+            for (int i = 0; i < U; ++i) v[i] = in ? __ldg(idx + (int64_t)(t + i) * f + j) : 0.0f;
+#pragma unroll
+            for (int i = 0; i < U; ++i) {
+                uint32_t b = __ballot_sync(0xffffffffu, v[i] > 0.0f);
+                if (tok_bits && lane == 0) tok_bits[(int64_t)(t + i) * W + w] = b;
+                seg |= b;
+                if ((t + i) % G == G - 1 || t + i == B - 1) {
+                    if (lane == 0) seg_bits[(int64_t)((t + i) / G) * W + w] = seg;
+                    seg = 0;
+                }
+            }
+        }
+        for (; t < B; ++t) {
+            float v = in ? __ldg(idx + (int64_t)t * f + j) : 0.0f;
+            uint32_t b = __ballot_sync(0xffffffffu, v > 0.0f);
+            if (tok_bits && lane == 0) tok_bits[(int64_t)t * W + w] = b;
+            seg |= b;
+            if (t % G == G - 1 || t == B - 1) {
+                if (lane == 0) seg_bits[(int64_t)(t / G) * W + w] = seg;
+                seg = 0;
+            }
+        }
+    }
+    if (zero_out) {
+        const int64_t n4 = zero_n / 4;
+        const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+        for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += stride)
+            reinterpret_cast<float4 *>(zero_out)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int64_t i = n4 * 4 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < zero_n; i += stride)
+            zero_out[i] = 0.0f;
+    }
+}
+
+constexpr int kCompactThreads = 1024;
+
+// CTA s compacts segment s.  act_cum[s] = number of active neurons in
+// segments 0..s (inclusive), the reference's cumulative convention
+// (cuda/kernel.cu:590-593).
+__global__ void __launch_bounds__(kCompactThreads)
+compact_kernel(const uint32_t *__restrict__ seg_bits, int W, int f, int32_t *__restrict__ merge_idx,
+               int32_t *__restrict__ act_cum, int32_t *__restrict__ counts) {
+    __shared__ int warp_tot[33];
+    __shared__ int prefix[kCompactThreads + 1];
+    __shared__ int before;
+    const int s = blockIdx.x;
+    // Active neurons of all earlier segments.
+    int acc = 0;
+    for (int64_t i = threadIdx.x; i < (int64_t)s * W; i += blockDim.x) acc += __popc(seg_bits[i]);
+    acc = __reduce_add_sync(0xffffffffu, acc);
+    if (threadIdx.x == 0) before = 0;
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) atomicAdd(&before, acc);
+
+    const uint32_t *bits = seg_bits + (int64_t)s * W;
+    int32_t *out = merge_idx + (int64_t)s * f;
+    int carry = 0;
+    for (int base = 0; base < W; base += kCompactThreads) {
+        const int n = min(kCompactThreads, W - base);
+        scan_popc(bits + base, n, prefix, warp_tot);
+        const int w = base + threadIdx.x;
+        if (threadIdx.x < n) {
+            uint32_t word = bits[w];
+            int p = carry + prefix[threadIdx.x];
+            while (word) {
+                int b = __ffs(word) - 1;
+                word &= word - 1;
+                out[p++] = w * 32 + b;
+            }
+        }
+        carry += prefix[n];
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) {
+        if (counts) counts[s] = carry;
+        if (act_cum) act_cum[s] = before + carry;
+    }
+}
+
+int launch_union_bits(const float *idx, int B, int f, int G, uint32_t *tok_bits, uint32_t *seg_bits,
+                      float *zero_out, int64_t zero_n, cudaStream_t st) {
+    const int W = words_of(f);
+    const int grid = (W + kUnionWarps - 1) / kUnionWarps;
+    union_bits_kernel<<<grid, kUnionWarps * 32, 0, st>>>(idx, B, f, W, G, tok_bits, seg_bits, zero_out, zero_n);
+    SPB_LAUNCH_CHECK("union_bits_kernel");
+    return SPB_OK;
+}
+
+int launch_compact(const uint32_t *seg_bits, int S, int f, int32_t *merge_idx, int32_t *act_cum, int32_t *counts,
+                   cudaStream_t st) {
+    compact_kernel<<<S, kCompactThreads, 0, st>>>(seg_bits, words_of(f), f, merge_idx, act_cum, counts);
+    SPB_LAUNCH_CHECK("compact_kernel");
+    return SPB_OK;
+}
+
+}  // namespace spb

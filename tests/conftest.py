@@ -1,0 +1,62 @@
+"""Shared test setup: markers, paths, lazily built libraries and GPU fixtures."""
+import os
+import sys
+
+import numpy as np
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, ROOT)
+sys.path.insert(0, os.path.join(ROOT, "oracle"))
+
+# FFN outputs: fp16 inputs with fp32 accumulation (benchmark contract).
+RTOL = 1e-2
+ATOL = 1e-3
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a CUDA device (B200); runs on the GPU host")
+
+
+@pytest.fixture(scope="session")
+def oracle_mod():
+    import oracle
+    oracle.build(ref=False)
+    return oracle
+
+
+@pytest.fixture(scope="session")
+def spb():
+    import spbatch_b200
+    if not os.path.exists(spbatch_b200.LIB_PATH):
+        from spbatch_b200 import build
+        build.build()
+    spbatch_b200.lib()
+    return spbatch_b200
+
+
+@pytest.fixture(scope="session")
+def cuda():
+    import torch
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    return torch.device("cuda:0")
+
+
+def assert_close(got, want, rtol=RTOL, atol=ATOL):
+    np.testing.assert_allclose(np.asarray(got, np.float64), np.asarray(want, np.float64), rtol=rtol, atol=atol)
+
+
+def golden_union_cases():
+    """Yields (name, labels [B][f] fp32, per-group counts, concatenated merge)
+    from tests/golden/union_ref.npz (outputs of the reference's
+    naive_sparsity_div)."""
+    z = np.load(os.path.join(ROOT, "tests", "golden", "union_ref.npz"))
+    names = sorted({k.split("/")[0] for k in z.files})
+    for n in names:
+        if f"{n}/labels" in z.files:
+            lab = z[f"{n}/labels"]
+        else:
+            B, f = z[f"{n}/shape"]
+            lab = np.unpackbits(z[f"{n}/bits"], axis=1)[:, :f].astype(np.float32)
+        yield n, lab, z[f"{n}/counts"], z[f"{n}/merge"]

@@ -1,0 +1,73 @@
+"""CPU tests of the C-ABI library: it loads, exports every symbol the public
+headers declare, and rejects bad arguments before touching a device."""
+import ctypes as C
+import os
+import re
+
+import pytest
+
+from conftest import ROOT
+
+
+def _declared(header, pattern):
+    src = open(os.path.join(ROOT, "include", header)).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    src = re.sub(r"//[^\n]*", "", src)
+    return sorted(set(re.findall(pattern, src, flags=re.M)))
+
+
+def test_c_abi_exports_everything_declared(spb):
+    names = _declared("spb.h", r"\b(spb_[a-z0-9_]+)\s*\(")
+    assert "spb_ffn_forward" in names and "spb_union" in names
+    for n in names:
+        assert hasattr(spb.lib(), n), f"{n} declared in include/spb.h but not exported"
+
+
+def test_dropin_api_exports_everything_declared(spb):
+    names = _declared("spbatch/kernel.cuh", r"^\s*void\s+([a-z0-9_]+)\s*\(")
+    names = [n for n in names if n != "die"]
+    assert len(names) == 17, names
+    for n in names:
+        assert n in spb.dropin._SYMS, f"{n} missing from the Python binding table"
+        sym = spb.dropin._SYMS[n][0]
+        assert hasattr(spb.lib(), sym), f"{n} ({sym}) not exported"
+
+
+def test_version_and_workspace(spb):
+    L = spb.lib()
+    assert L.spb_version() >= 1
+    assert L.spb_ffn_workspace_bytes(0, 4096, 11008, 0) == 0
+    a = L.spb_ffn_workspace_bytes(1, 4096, 11008, 0)
+    b = L.spb_ffn_workspace_bytes(32, 4096, 11008, 0)
+    c = L.spb_ffn_workspace_bytes(32, 4096, 11008, 8)
+    assert 0 < a < b < c
+    assert a % 256 == 0
+
+
+def test_invalid_arguments_fail_without_device(spb):
+    L = spb.lib()
+    rc = L.spb_ffn_forward(None, None, None, 0, None, None, 1, 4096, 11008, 0, 1, 0, None, None, None, None, 0,
+                           None)
+    assert rc == 1
+    assert b"null" in L.spb_last_error()
+    fake = C.c_void_p(256)  # never dereferenced: shape checks fail first
+    rc = L.spb_ffn_forward(fake, fake, fake, 0, fake, fake, 1, 100, 11008, 0, 1, 0, fake, None, None, fake, 1 << 30,
+                           None)
+    assert rc == 1 and b"multiple of 64" in L.spb_last_error()
+    rc = L.spb_ffn_forward(fake, fake, fake, 7, fake, fake, 1, 4096, 11008, 0, 1, 0, fake, None, None, fake,
+                           1 << 30, None)
+    assert rc == 1 and b"weight type" in L.spb_last_error()
+    rc = L.spb_ffn_forward(fake, fake, fake, 0, fake, fake, 1, 4096, 11008, 0, 1, 0, fake, None, None, fake, 16,
+                           None)
+    assert rc == 2 and b"workspace" in L.spb_last_error()
+    rc = L.spb_union(None, 8, 64, 8, None, None, None, None, 0, None)
+    assert rc == 1
+    rc = L.spb_union(fake, 8, 64, -1, fake, fake, None, fake, 1 << 20, None)
+    assert rc == 1
+
+
+def test_python_wrappers_refuse_cpu_tensors(spb):
+    import torch
+    x = torch.zeros(2, 64)
+    with pytest.raises(spb.SpbError):
+        spb.ffn_forward(x, x, x, x, x)

@@ -1,0 +1,192 @@
+"""The reference's C++ API (include/spbatch/kernel.cuh) served by the B200
+library, called through its mangled C++ symbols exactly as the reference's
+drivers call it (cuda/ffn_test.cu MLP_BS / MLP_naive), checked against the
+oracle and, where oracle/_ref was built, against the reference's own kernels
+run on the same GPU."""
+import numpy as np
+import pytest
+
+from conftest import assert_close
+from spbatch_b200.workload import zipf_active_labels
+
+pytestmark = pytest.mark.gpu
+
+
+def _dev(a, dev):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+
+
+def _stream():
+    import torch
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _mlp_bs(spb, library, cuda, W, x, lab, act="relu_and_mul_cuda"):
+    """MLP_BS (cuda/ffn_test.cu:129-142) through the C++ API of `library`."""
+    import torch
+    wg, wu, wd = W
+    B, d = x.shape
+    f = lab.shape[1]
+    groups = B // 8
+    F = lambda n: spb.dropin.fn(n, library)  # noqa: E731
+    merge = torch.zeros(groups * f, dtype=torch.int32, device=cuda)
+    act_n = torch.zeros(groups, dtype=torch.int32, device=cuda)
+    gate = torch.zeros(B, f, device=cuda)
+    up = torch.zeros(B, f, device=cuda)
+    h = torch.zeros(B, f, device=cuda)
+    out = torch.full((B, d), 7.0, device=cuda)
+    s = _stream()
+    F("get_idx_cuda")(lab.data_ptr(), merge.data_ptr(), act_n.data_ptr(), B, f, s)
+    F("gate_and_up_mul_mat_cuda_sparse")(wg.data_ptr(), wu.data_ptr(), x.data_ptr(), gate.data_ptr(),
+                                         up.data_ptr(), merge.data_ptr(), f, B, d, act_n.data_ptr(), s, s)
+    F(act)(gate.data_ptr(), up.data_ptr(), h.data_ptr(), B, f, s)
+    F("down_mul_mat_cuda_sparse")(wd.data_ptr(), h.data_ptr(), out.data_ptr(), merge.data_ptr(), d, B, f,
+                                  act_n.data_ptr(), s)
+    torch.cuda.synchronize()
+    return dict(merge=merge.cpu().numpy().reshape(groups, f), act=act_n.cpu().numpy(), gate=gate.cpu().numpy(),
+                up=up.cpu().numpy(), out=out.cpu().numpy())
+
+
+def _inputs(cuda, B, d, f, k, seed):
+    rng = np.random.default_rng(seed)
+    W = [(rng.standard_normal((f, d)) * 0.02).astype(np.float16) for _ in range(3)]
+    x = rng.standard_normal((B, d)).astype(np.float32)
+    lab = zipf_active_labels(B, f, k, seed=seed)
+    return W, x, lab, [_dev(w, cuda) for w in W], _dev(x, cuda), _dev(lab, cuda)
+
+
+@pytest.mark.parametrize("act", ["relu_and_mul_cuda", "relu_relu_mul_cuda"])
+def test_mlp_bs_dropin_vs_oracle(spb, cuda, oracle_mod, act):
+    B, d, f = 16, 4096, 11008
+    W, x, lab, Wd, xd, labd = _inputs(cuda, B, d, f, 1101, 5)
+    r = _mlp_bs(spb, None, cuda, Wd, xd, labd, act)
+    merge, counts = oracle_mod.union(lab, 8)
+    np.testing.assert_array_equal(r["act"], np.cumsum(counts))
+    for g in range(2):
+        np.testing.assert_array_equal(r["merge"][g, :counts[g]], merge[g, :counts[g]])
+    g_ref = oracle_mod.up_compact(W[0], x, merge, counts, 8)
+    u_ref = oracle_mod.up_compact(W[1], x, merge, counts, 8)
+    for t in range(B):
+        n = counts[t // 8]
+        assert_close(r["gate"][t, :n], g_ref[t, :n])
+        assert_close(r["up"][t, :n], u_ref[t, :n])
+    want = oracle_mod.ffn(*W, x, lab, G=8, per_token=False, act=1 if act == "relu_relu_mul_cuda" else 0)
+    assert_close(r["out"], want)
+
+
+def test_mlp_bs_matches_reference_library(spb, cuda, oracle_mod):
+    """Same inputs through the reference's own MLP_BS kernels (rebuilt for
+    sm_100a in oracle/_ref) and through ours."""
+    ref = oracle_mod.ref_lib()
+    if ref is None:
+        pytest.skip("oracle/_ref not built")
+    B, d, f = 16, 4096, 11008
+    W, x, lab, Wd, xd, labd = _inputs(cuda, B, d, f, 1101, 6)
+    ours = _mlp_bs(spb, None, cuda, Wd, xd, labd)
+    theirs = _mlp_bs(spb, ref, cuda, Wd, xd, labd)
+    np.testing.assert_array_equal(ours["act"], theirs["act"])
+    for g in range(2):
+        n = ours["act"][g] - (ours["act"][g - 1] if g else 0)
+        np.testing.assert_array_equal(ours["merge"][g, :n], theirs["merge"][g, :n])
+    assert_close(ours["out"], theirs["out"])
+
+
+def test_naive_mlp_pins_oracle(spb, cuda, oracle_mod):
+    """MLP_naive (cuda/ffn_test.cu:144-163) with the reference's own naive
+    kernels pins the oracle's unrounded gather GEMMs; ours must agree too."""
+    import torch
+    B, d, f = 8, 1024, 2048
+    W, x, lab, Wd, xd, labd = _inputs(cuda, B, d, f, 300, 7)
+    merge, counts = oracle_mod.union(lab, 8)
+    want_g = oracle_mod.up_compact(W[0], x, merge, counts, 8, round_x=False)
+    libs = [None] + ([oracle_mod.ref_lib()] if oracle_mod.ref_lib() is not None else [])
+    for library in libs:
+        F = lambda n: spb.dropin.fn(n, library)  # noqa: E731
+        s = _stream()
+        m = torch.zeros(f, dtype=torch.int32, device=cuda)
+        a = torch.zeros(1, dtype=torch.int32, device=cuda)
+        F("get_idx_cuda")(labd.data_ptr(), m.data_ptr(), a.data_ptr(), B, f, s)
+        g = torch.zeros(B, f, device=cuda)
+        F("naive_mm_up_cuda")(Wd[0].data_ptr(), xd.data_ptr(), g.data_ptr(), f, B, d, a.data_ptr(), m.data_ptr(), s)
+        hh = torch.relu(g) * 0.5
+        o = torch.zeros(B, d, device=cuda)
+        F("naive_mm_down_cuda")(Wd[2].data_ptr(), hh.data_ptr(), o.data_ptr(), d, B, f, a.data_ptr(), m.data_ptr(), s)
+        torch.cuda.synchronize()
+        n = counts[0]
+        assert_close(g.cpu().numpy()[:, :n], want_g[:, :n], rtol=1e-4, atol=1e-4)
+        want_o = oracle_mod.down_compact(W[2], hh.cpu().numpy(), merge, counts, 8, round_h=False)
+        assert_close(o.cpu().numpy(), want_o, rtol=1e-4, atol=1e-4)
+
+
+def test_powerinfer_gemv_and_axpy(spb, cuda):
+    import torch
+    rng = np.random.default_rng(8)
+    B, d, f = 4, 512, 1024
+    w = (rng.standard_normal((f, d)) * 0.05).astype(np.float16)
+    y = rng.standard_normal((B, d)).astype(np.float32)
+    idx = rng.standard_normal((B, f)).astype(np.float32)
+    idx[:, ::5] = 0.0
+    dst = torch.full((B, f), 1.0, device=cuda)
+    spb.dropin.fn("convert_mul_mat_batch_f16_cuda_sparse")(
+        _dev(w, cuda).data_ptr(), _dev(y, cuda).data_ptr(), dst.data_ptr(), d, f, B, f, _stream(), None,
+        _dev(idx, cuda).data_ptr())
+    want = 1.0 + np.where(idx > 0, y @ w.astype(np.float32).T, 0.0)
+    torch.cuda.synchronize()
+    assert_close(dst.cpu().numpy(), want)
+    # axpy: W_down stored [f][d]; h [B][f]; token active when idx >= 0
+    h = rng.standard_normal((B, f)).astype(np.float32)
+    out = torch.zeros(B, d, device=cuda)
+    spb.dropin.fn("convert_axpy_sparse_batch_f16_cuda")(
+        _dev(w, cuda).data_ptr(), _dev(h, cuda).data_ptr(), out.data_ptr(), d, f, f, B, _stream(), None,
+        _dev(idx, cuda).data_ptr())
+    torch.cuda.synchronize()
+    want = np.where(idx >= 0, h, 0.0) @ w.astype(np.float32)
+    assert_close(out.cpu().numpy(), want)
+
+
+def test_elementwise_and_dense(spb, cuda):
+    import torch
+    rng = np.random.default_rng(10)
+    a = rng.standard_normal(1000).astype(np.float32)
+    b = rng.standard_normal(1000).astype(np.float32)
+    A, Bv = _dev(a, cuda), _dev(b, cuda)
+    o = torch.zeros(1000, device=cuda)
+    s = _stream()
+    spb.dropin.fn("relu_f32_cuda")(A.data_ptr(), o.data_ptr(), 1000, s)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(o.cpu().numpy(), np.maximum(a, 0))
+    spb.dropin.fn("mul_f32_cuda")(A.data_ptr(), Bv.data_ptr(), o.data_ptr(), 1000, 100, s)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(o.cpu().numpy(), a * b[np.arange(1000) % 100])
+    hbuf = torch.zeros(1000, dtype=torch.float16, device=cuda)
+    spb.dropin.fn("convert_fp32_to_fp16_cuda")(A.data_ptr(), hbuf.data_ptr(), 1000, s)
+    spb.dropin.fn("convert_fp16_to_fp32_cuda")(hbuf.data_ptr(), o.data_ptr(), 1000, s)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(o.cpu().numpy(), a.astype(np.float16).astype(np.float32))
+    M, N, K = 96, 40, 200
+    am = (rng.standard_normal((M, K)) * 0.1).astype(np.float16)
+    bm = rng.standard_normal((N, K)).astype(np.float32)
+    c = torch.zeros(M, N, device=cuda)
+    spb.dropin.fn("gemm_cuda")(_dev(am, cuda).data_ptr(), _dev(bm, cuda).data_ptr(), c.data_ptr(), M, N, K, s)
+    torch.cuda.synchronize()
+    assert_close(c.cpu().numpy(), am.astype(np.float32) @ bm.astype(np.float16).astype(np.float32).T)
+
+
+def test_add_sparse(spb, cuda, oracle_mod):
+    import torch
+    rng = np.random.default_rng(12)
+    B, f = 16, 512
+    lab = (rng.random((B, f)) < 0.1).astype(np.float32)
+    merge, counts = oracle_mod.union(lab, 8)
+    act = torch.tensor(np.cumsum(counts), dtype=torch.int32, device=cuda)
+    a = rng.standard_normal((B, f)).astype(np.float32)
+    bias = rng.standard_normal(f).astype(np.float16)
+    c = torch.zeros(B, f, device=cuda)
+    spb.dropin.fn("add_sparse_cuda")(_dev(a, cuda).data_ptr(), _dev(bias, cuda).data_ptr(), c.data_ptr(), f, B,
+                                     act.data_ptr(), _dev(merge, cuda).data_ptr(), _stream())
+    torch.cuda.synchronize()
+    c = c.cpu().numpy()
+    for t in range(B):
+        n = counts[t // 8]
+        np.testing.assert_allclose(c[t, :n], a[t, :n] + bias[merge[t // 8, :n]].astype(np.float32), rtol=1e-6)

@@ -1,0 +1,98 @@
+"""GPU parity of the fused sparse-FFN path against the CPU oracle
+(rel 1e-2 / abs 1e-3 for fp16 weights with fp32 accumulation; union
+indices bit-exact)."""
+import numpy as np
+import pytest
+
+from conftest import assert_close
+from spbatch_b200.workload import zipf_active_labels
+
+pytestmark = pytest.mark.gpu
+
+
+def _dev(a, dev):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+
+
+def _layer(rng, d, f, std=0.02):
+    return [(rng.standard_normal((f, d)) * std).astype(np.float16) for _ in range(3)]
+
+
+def _run(spb, cuda, wg, wu, wd, x, lab, **kw):
+    import torch
+    f = lab.shape[1]
+    merge = torch.full((f,), -1, dtype=torch.int32, device=cuda)
+    count = torch.zeros(1, dtype=torch.int32, device=cuda)
+    out = spb.ffn_forward(_dev(wg, cuda), _dev(wu, cuda), _dev(wd, cuda), _dev(x, cuda), _dev(lab, cuda),
+                          merge_idx_out=merge, count_out=count, **kw)
+    torch.cuda.synchronize()
+    return out.cpu().numpy(), merge.cpu().numpy(), int(count.cpu()[0])
+
+
+@pytest.mark.parametrize("B", [1, 2, 3, 4])
+@pytest.mark.parametrize("per_token", [True, False])
+def test_gemv_path_small(spb, cuda, oracle_mod, B, per_token):
+    rng = np.random.default_rng(100 + B)
+    d, f = 256, 640
+    wg, wu, wd = _layer(rng, d, f, 0.05)
+    x = rng.standard_normal((B, d)).astype(np.float32)
+    lab = (rng.random((B, f)) < 0.15).astype(np.float32)
+    out, merge, U = _run(spb, cuda, wg, wu, wd, x, lab, per_token_mask=per_token, path=spb.PATH_GEMV)
+    want = oracle_mod.ffn(wg, wu, wd, x, lab, per_token=per_token)
+    assert_close(out, want)
+    m_ref, c_ref = oracle_mod.union(lab, B)
+    assert U == c_ref[0]
+    np.testing.assert_array_equal(merge[:U], m_ref[0, :U])
+
+
+@pytest.mark.parametrize("act", [0, 1])
+def test_gemv_path_7b_b1(spb, cuda, oracle_mod, act):
+    """Config 1 shape: 7B layer, one token, exactly 1101 active neurons."""
+    rng = np.random.default_rng(0)
+    d, f = 4096, 11008
+    wg, wu, wd = _layer(rng, d, f)
+    x = rng.standard_normal((1, d)).astype(np.float32)
+    lab = zipf_active_labels(1, f, 1101, seed=0)
+    out, merge, U = _run(spb, cuda, wg, wu, wd, x, lab, act=act, path=spb.PATH_GEMV)
+    assert U == 1101
+    np.testing.assert_array_equal(merge[:U], np.nonzero(lab[0])[0])
+    assert_close(out, oracle_mod.ffn(wg, wu, wd, x, lab, act=act))
+
+
+@pytest.mark.parametrize("B", [2, 4])
+def test_gemv_path_13b_zipf(spb, cuda, oracle_mod, B):
+    rng = np.random.default_rng(1)
+    d, f = 5120, 13824
+    wg, wu, wd = _layer(rng, d, f)
+    x = rng.standard_normal((B, d)).astype(np.float32)
+    lab = zipf_active_labels(B, f, 1106, seed=1)
+    out, merge, U = _run(spb, cuda, wg, wu, wd, x, lab, path=spb.PATH_GEMV)
+    assert_close(out, oracle_mod.ffn(wg, wu, wd, x, lab))
+
+
+def test_empty_union_gives_zero(spb, cuda):
+    rng = np.random.default_rng(2)
+    d, f = 512, 1024
+    wg, wu, wd = _layer(rng, d, f)
+    x = rng.standard_normal((2, d)).astype(np.float32)
+    lab = np.zeros((2, f), np.float32)
+    out, _, U = _run(spb, cuda, wg, wu, wd, x, lab, path=spb.PATH_GEMV)
+    assert U == 0 and not out.any()
+
+
+def test_repeated_calls_reuse_workspace(spb, cuda, oracle_mod):
+    """Workspace contents from one call must not leak into the next."""
+    import torch
+    rng = np.random.default_rng(3)
+    d, f = 1024, 2048
+    wg, wu, wd = _layer(rng, d, f)
+    ws = spb.new_workspace(4, d, f, 0, cuda)
+    W = [_dev(w, cuda) for w in (wg, wu, wd)]
+    for it in range(3):
+        B = [4, 1, 3][it]
+        x = rng.standard_normal((B, d)).astype(np.float32)
+        lab = (rng.random((B, f)) < [0.3, 0.01, 0.1][it]).astype(np.float32)
+        out = spb.ffn_forward(*W, _dev(x, cuda), _dev(lab, cuda), workspace=ws, path=spb.PATH_GEMV)
+        torch.cuda.synchronize()
+        assert_close(out.cpu().numpy(), oracle_mod.ffn(wg, wu, wd, x, lab))
