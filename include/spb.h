@@ -6,6 +6,9 @@
  * synchronisation and returns an spb_status; spb_last_error() describes the
  * last failure on the calling thread.  Scratch memory comes from a
  * caller-owned device workspace whose size spb_ffn_workspace_bytes() reports.
+ * The first 4 bytes of a workspace hold a sticky device error code (0 = no
+ * error): kernels whose bounded waits run out record a code there and return
+ * instead of hanging the GPU; only the caller clears it.
  *
  * Each entry point names the reference interface it replaces
  * (cuda/kernel.cuh / cuda/kernel.cu of SMAC-Zhang/SpBatch).  The reference's
@@ -98,6 +101,9 @@ int spb_ffn_forward(const void *w_gate, const void *w_up, const void *w_down, in
                     const float *idx, int B, int d, int f, int act, int per_token_mask, int path, float *out,
                     int32_t *merge_idx_out, int32_t *count_out, void *workspace, size_t workspace_bytes,
                     void *stream);
+
+/* Kernel launches one spb_ffn_forward call makes for batch B and `path`. */
+int spb_ffn_launches(int B, int path);
 
 #ifdef __cplusplus
 }

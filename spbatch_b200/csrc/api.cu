@@ -57,6 +57,8 @@ int ensure_smem(const void *kernel, size_t bytes) {
     return SPB_OK;
 }
 
+constexpr int kGemvMaxBatch = 4;
+
 static bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 }  // namespace spb
@@ -83,7 +85,7 @@ int spb_union(const float *idx, int B, int f, int group, int32_t *merge_idx, int
     Workspace ws = carve_workspace(workspace, B, 0, f, group);
     if (!workspace || workspace_bytes < ws.bytes) return fail(SPB_ERR_WORKSPACE, "spb_union: workspace too small");
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    int rc = launch_union_bits(idx, B, f, G, tok_bits, ws.seg_bits, nullptr, 0, st);
+    int rc = launch_union_bits(idx, B, f, G, tok_bits, ws.seg_bits, PrepJobs{}, st);
     if (rc) return rc;
     return launch_compact(ws.seg_bits, S, f, merge_idx, act_cum, ws.counts, st);
 }
@@ -95,6 +97,7 @@ int spb_ffn_forward(const void *w_gate, const void *w_up, const void *w_down, in
     if (!w_gate || !w_up || !w_down || !x || !idx || !out) return fail(SPB_ERR_INVALID, "spb_ffn_forward: null pointer");
     if (B <= 0 || d <= 0 || f <= 0) return fail(SPB_ERR_INVALID, "spb_ffn_forward: bad shape");
     if (d % 64 != 0) return fail(SPB_ERR_INVALID, "spb_ffn_forward: d must be a multiple of 64");
+    if (B > 256) return fail(SPB_ERR_UNSUPPORTED, "spb_ffn_forward: B > 256");
     if (wtype != SPB_W_F16 && wtype != SPB_W_Q8_0 && wtype != SPB_W_Q4_0)
         return fail(SPB_ERR_INVALID, "spb_ffn_forward: unknown weight type");
     if (act != SPB_ACT_RELU_MUL && act != SPB_ACT_RELU_RELU_MUL)
@@ -107,10 +110,58 @@ int spb_ffn_forward(const void *w_gate, const void *w_up, const void *w_down, in
         return fail(SPB_ERR_WORKSPACE, "spb_ffn_forward: workspace too small");
     cudaStream_t st = static_cast<cudaStream_t>(stream);
 
-    if (path == SPB_PATH_AUTO) path = SPB_PATH_GEMV;
-    if (path != SPB_PATH_GEMV) return fail(SPB_ERR_UNSUPPORTED, "spb_ffn_forward: tensor path not built yet");
+    if (path == SPB_PATH_AUTO) path = B <= kGemvMaxBatch ? SPB_PATH_GEMV : SPB_PATH_TENSOR;
+    int32_t *merge = merge_idx_out ? merge_idx_out : ws.merge_idx;
+    int32_t *count = count_out ? count_out : ws.counts;
 
-    int rc = launch_union_bits(idx, B, f, B, ws.tok_bits, ws.seg_bits, out, (int64_t)B * d, st);
+    if (path == SPB_PATH_TENSOR) {
+        if (wtype != SPB_W_F16) return fail(SPB_ERR_UNSUPPORTED, "spb_ffn_forward: tensor path serves fp16 weights");
+        if (B > 256) return fail(SPB_ERR_UNSUPPORTED, "spb_ffn_forward: tensor path serves B <= 256");
+        if (d % 128 != 0) return fail(SPB_ERR_INVALID, "spb_ffn_forward: tensor path needs d % 128 == 0");
+        PrepJobs jobs;
+        jobs.zero_out = out;
+        jobs.zero_n = (int64_t)B * d;
+        jobs.zero_u32 = ws.tile_cnt;
+        jobs.zero_u32_n = 2 * (int64_t)ws.T;
+        jobs.x = x;
+        jobs.x16 = ws.x16;
+        jobs.B = B;
+        jobs.Np = ws.Np;
+        jobs.d = d;
+        int rc = launch_union_bits(idx, B, f, B, ws.tok_bits, ws.seg_bits, jobs, st);
+        if (rc) return rc;
+        TcLaunch L{};
+        L.wg = w_gate;
+        L.wu = w_up;
+        L.wd = w_down;
+        L.x16 = ws.x16;
+        L.h16 = ws.h16;
+        L.seg_bits = ws.seg_bits;
+        L.tok_bits = ws.tok_bits;
+        L.out = out;
+        L.merge_out = merge;
+        L.count_out = count;
+        L.partial = ws.partial;
+        L.tile_cnt = ws.tile_cnt;
+        L.tile_ready = ws.tile_ready;
+        L.err = ws.err;
+        L.B = B;
+        L.Np = ws.Np;
+        L.d = d;
+        L.f = f;
+        L.fpad = ws.fpad;
+        L.act = act;
+        L.per_token = per_token_mask;
+        L.grid = num_sms() < kMaxTcGrid ? num_sms() : kMaxTcGrid;
+        return launch_ffn_tc(L, st);
+    }
+    if (path != SPB_PATH_GEMV) return fail(SPB_ERR_INVALID, "spb_ffn_forward: unknown path");
+    if (B > kGemvMaxBatch) return fail(SPB_ERR_UNSUPPORTED, "spb_ffn_forward: CUDA-core path serves B <= 4");
+
+    PrepJobs jobs;
+    jobs.zero_out = out;
+    jobs.zero_n = (int64_t)B * d;
+    int rc = launch_union_bits(idx, B, f, B, ws.tok_bits, ws.seg_bits, jobs, st);
     if (rc) return rc;
     FusedGemvArgs a{};
     a.wg = w_gate;
@@ -126,10 +177,15 @@ int spb_ffn_forward(const void *w_gate, const void *w_up, const void *w_down, in
     a.act = act;
     a.per_token = per_token_mask;
     a.h = ws.h;
-    a.merge = merge_idx_out ? merge_idx_out : ws.merge_idx;
-    a.count = count_out ? count_out : ws.counts;
+    a.merge = merge;
+    a.count = count;
     a.out = out;
     return launch_fused_gemv(a, st);
+}
+
+int spb_ffn_launches(int B, int path) {
+    if (path == SPB_PATH_AUTO) path = B <= kGemvMaxBatch ? SPB_PATH_GEMV : SPB_PATH_TENSOR;
+    return path == SPB_PATH_TENSOR ? 2 : 3;
 }
 
 }  // extern "C"

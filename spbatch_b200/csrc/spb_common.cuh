@@ -37,15 +37,25 @@ int ensure_smem(const void *kernel, size_t bytes);
     } while (0)
 
 // ---- workspace layout ---------------------------------------------------
-// All regions are 256-byte aligned slices of one caller-owned buffer.
+// All regions are 256-byte aligned slices of one caller-owned buffer.  The
+// first 4 bytes hold a sticky device error code (0 = none) that kernels set
+// instead of trapping when a bounded wait runs out; nothing clears it but the
+// caller.
+constexpr int kMaxTcGrid = 160;  // upper bound on the tensor-path grid (148 SMs on B200)
+
 struct Workspace {
-    uint32_t *tok_bits;  // [B][W] per-token activity bits
-    uint32_t *seg_bits;  // [S][W] per-segment union bits
-    int32_t *merge_idx;  // [S][f] compacted ascending neuron ids
-    int32_t *counts;     // [S + 1] per-segment counts (+1 spare)
-    __half *h;           // [f][B] fp16 intermediate, compacted positions x tokens
-    float *partial;      // [2][f][B] fp32 partial gate/up sums (split-K)
-    uint32_t *sync;      // [64] counters / flags, kept zero between launches
+    uint32_t *err;         // [1] sticky device error code
+    uint32_t *tile_cnt;    // [T] per-tile split-K arrival counters (zeroed per launch)
+    uint32_t *tile_ready;  // [T] per-tile "h published" flags (zeroed per launch)
+    uint32_t *tok_bits;    // [B][W] per-token activity bits
+    uint32_t *seg_bits;    // [S][W] per-segment union bits
+    int32_t *merge_idx;    // [S][f] compacted ascending neuron ids
+    int32_t *counts;       // [S + 1] per-segment counts (+1 spare)
+    __half *h;             // [f][B] fp16 intermediate of the CUDA-core path
+    __half *x16;           // [Np][d] fp16 activations of the tensor path
+    __half *h16;           // [Np][fpad] fp16 h of the tensor path (K-major)
+    float *partial;        // [kMaxTcGrid][2][Np][128] split-K partial sums
+    int T, Np, fpad;
     size_t bytes;
 };
 
@@ -53,25 +63,37 @@ inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
 __host__ __device__ inline int words_of(int f) { return (f + 31) / 32; }
 
+// MMA N extent for a batch of B tokens: a multiple of 16 in [16, 256].
+inline int padded_batch(int B) { return B <= 16 ? 16 : ((B + 15) / 16) * 16; }
+
 // Lays the workspace out over `base` (nullptr: only compute the size).
 inline Workspace carve_workspace(void *base, int B, int d, int f, int group) {
-    (void)d;
     int S = group <= 0 ? 1 : (B + group - 1) / group;
     int W = words_of(f);
     Workspace w{};
+    w.T = (f + 127) / 128;
+    w.fpad = w.T * 128;
+    w.Np = B <= 256 ? padded_batch(B) : 0;
     size_t off = 0;
     auto take = [&](size_t n) {
         size_t o = off;
         off += align256(n);
         return base ? (void *)((char *)base + o) : nullptr;
     };
+    uint32_t *sync = (uint32_t *)take(sizeof(uint32_t) * (64 + 2 * (size_t)w.T));
+    w.err = sync;
+    w.tile_cnt = sync ? sync + 64 : nullptr;
+    w.tile_ready = sync ? sync + 64 + w.T : nullptr;
     w.tok_bits = (uint32_t *)take(sizeof(uint32_t) * (size_t)B * W);
     w.seg_bits = (uint32_t *)take(sizeof(uint32_t) * (size_t)S * W);
     w.merge_idx = (int32_t *)take(sizeof(int32_t) * (size_t)S * f);
     w.counts = (int32_t *)take(sizeof(int32_t) * (size_t)(S + 1));
     w.h = (__half *)take(sizeof(__half) * (size_t)f * B);
-    w.partial = (float *)take(sizeof(float) * 2 * (size_t)f * B);
-    w.sync = (uint32_t *)take(sizeof(uint32_t) * 64);
+    if (d > 0 && w.Np > 0) {
+        w.x16 = (__half *)take(sizeof(__half) * (size_t)w.Np * d);
+        w.h16 = (__half *)take(sizeof(__half) * (size_t)w.Np * w.fpad);
+        w.partial = (float *)take(sizeof(float) * (size_t)kMaxTcGrid * 2 * w.Np * 128);
+    }
     w.bytes = off;
     return w;
 }

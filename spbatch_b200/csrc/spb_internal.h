@@ -7,8 +7,21 @@
 namespace spb {
 
 // union.cu
+// Optional work folded into the union launch so the layer needs no extra
+// launches: zero the fp32 output the down projection accumulates into, zero
+// the cross-CTA tile counters/flags, and write the fp16 copy of x (rows padded
+// with zeros to Np) that the tensor-core path reads.
+struct PrepJobs {
+    float *zero_out = nullptr;
+    int64_t zero_n = 0;
+    uint32_t *zero_u32 = nullptr;
+    int64_t zero_u32_n = 0;
+    const float *x = nullptr;
+    __half *x16 = nullptr;
+    int B = 0, Np = 0, d = 0;
+};
 int launch_union_bits(const float *idx, int B, int f, int G, uint32_t *tok_bits, uint32_t *seg_bits,
-                      float *zero_out, int64_t zero_n, cudaStream_t st);
+                      const PrepJobs &jobs, cudaStream_t st);
 int launch_compact(const uint32_t *seg_bits, int S, int f, int32_t *merge_idx, int32_t *act_cum, int32_t *counts,
                    cudaStream_t st);
 
@@ -34,5 +47,19 @@ int launch_dropin_up(const __half *wg, const __half *wu, const float *x, float *
                      const int32_t *merge_idx, const int32_t *act_cum, int B, int d, int f, int G, cudaStream_t st);
 int launch_dropin_down(const __half *wd, const float *h, float *out, const int32_t *merge_idx,
                        const int32_t *act_cum, int B, int d, int f, int G, cudaStream_t st);
+
+// tc_ffn.cu -- tcgen05 tensor-core path (one persistent launch after the union)
+struct TcLaunch {
+    const void *wg, *wu, *wd;
+    const __half *x16;
+    __half *h16;
+    const uint32_t *seg_bits, *tok_bits;
+    float *out;
+    int32_t *merge_out, *count_out;
+    float *partial;
+    uint32_t *tile_cnt, *tile_ready, *err;
+    int B, Np, d, f, fpad, act, per_token, grid;
+};
+int launch_ffn_tc(const TcLaunch &L, cudaStream_t st);
 
 }  // namespace spb

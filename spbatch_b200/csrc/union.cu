@@ -24,7 +24,10 @@ constexpr int kUnionWarps = 8;
 
 __global__ void __launch_bounds__(kUnionWarps * 32)
 union_bits_kernel(const float *__restrict__ idx, int B, int f, int W, int G, uint32_t *__restrict__ tok_bits,
-                  uint32_t *__restrict__ seg_bits, float *__restrict__ zero_out, int64_t zero_n) {
+                  uint32_t *__restrict__ seg_bits, PrepJobs jobs) {
+    // Let a dependent launch (programmatic dependent launch) start its
+    // prologue now; it still waits for this grid's results before reading them.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int lane = threadIdx.x & 31;
     const int w = blockIdx.x * kUnionWarps + (threadIdx.x >> 5);
     if (w < W) {
@@ -59,13 +62,25 @@ union_bits_kernel(const float *__restrict__ idx, int B, int f, int W, int G, uin
             }
         }
     }
-    if (zero_out) {
-        const int64_t n4 = zero_n / 4;
-        const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-        for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += stride)
-            reinterpret_cast<float4 *>(zero_out)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int64_t i = n4 * 4 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < zero_n; i += stride)
-            zero_out[i] = 0.0f;
+    const int64_t gtid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    if (jobs.zero_out) {
+        const int64_t n4 = jobs.zero_n / 4;
+        for (int64_t i = gtid; i < n4; i += stride)
+            reinterpret_cast<float4 *>(jobs.zero_out)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int64_t i = n4 * 4 + gtid; i < jobs.zero_n; i += stride) jobs.zero_out[i] = 0.0f;
+    }
+    if (jobs.zero_u32)
+        for (int64_t i = gtid; i < jobs.zero_u32_n; i += stride) jobs.zero_u32[i] = 0u;
+    if (jobs.x16) {
+        // fp16 copy of x, rows padded with zeros to Np (the MMA N extent)
+        const int64_t n2 = (int64_t)jobs.Np * jobs.d / 2;
+        for (int64_t i = gtid; i < n2; i += stride) {
+            const int64_t e = 2 * i;
+            const int t = (int)(e / jobs.d);
+            float2 v = t < jobs.B ? *reinterpret_cast<const float2 *>(jobs.x + e) : make_float2(0.f, 0.f);
+            reinterpret_cast<__half2 *>(jobs.x16)[i] = __floats2half2_rn(v.x, v.y);
+        }
     }
 }
 
@@ -115,10 +130,11 @@ compact_kernel(const uint32_t *__restrict__ seg_bits, int W, int f, int32_t *__r
 }
 
 int launch_union_bits(const float *idx, int B, int f, int G, uint32_t *tok_bits, uint32_t *seg_bits,
-                      float *zero_out, int64_t zero_n, cudaStream_t st) {
+                      const PrepJobs &jobs, cudaStream_t st) {
     const int W = words_of(f);
-    const int grid = (W + kUnionWarps - 1) / kUnionWarps;
-    union_bits_kernel<<<grid, kUnionWarps * 32, 0, st>>>(idx, B, f, W, G, tok_bits, seg_bits, zero_out, zero_n);
+    int grid = (W + kUnionWarps - 1) / kUnionWarps;
+    if (jobs.x16 || jobs.zero_out) grid = max(grid, num_sms());
+    union_bits_kernel<<<grid, kUnionWarps * 32, 0, st>>>(idx, B, f, W, G, tok_bits, seg_bits, jobs);
     SPB_LAUNCH_CHECK("union_bits_kernel");
     return SPB_OK;
 }

@@ -89,7 +89,18 @@ def test_mlp_bs_matches_reference_library(spb, cuda, oracle_mod):
     for g in range(2):
         n = ours["act"][g] - (ours["act"][g - 1] if g else 0)
         np.testing.assert_array_equal(ours["merge"][g, :n], theirs["merge"][g, :n])
-    assert_close(ours["out"], theirs["out"])
+        for t in range(8 * g, 8 * g + 8):
+            assert_close(ours["gate"][t, :n], theirs["gate"][t, :n])
+            assert_close(ours["up"][t, :n], theirs["up"][t, :n])
+    # The reference's mm_up writes whole 256-row tiles, so compacted slots past
+    # the group's count hold values computed from stale shared memory
+    # (cuda/kernel.cu:129-135, 694-702); mm_down then multiplies its zero-filled
+    # weight rows by those h columns (cuda/kernel.cu:182-193, 757-800), and a
+    # non-finite stale value turns whole outputs into NaN.  Compare the
+    # outputs the reference did produce as finite numbers.
+    fin = np.isfinite(theirs["out"])
+    if fin.any():
+        assert_close(ours["out"][fin], theirs["out"][fin])
 
 
 def test_naive_mlp_pins_oracle(spb, cuda, oracle_mod):

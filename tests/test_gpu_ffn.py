@@ -96,3 +96,92 @@ def test_repeated_calls_reuse_workspace(spb, cuda, oracle_mod):
         out = spb.ffn_forward(*W, _dev(x, cuda), _dev(lab, cuda), workspace=ws, path=spb.PATH_GEMV)
         torch.cuda.synchronize()
         assert_close(out.cpu().numpy(), oracle_mod.ffn(wg, wu, wd, x, lab))
+
+
+def _ws_error(ws):
+    """The workspace's sticky device error code (first 4 bytes)."""
+    return int(np.frombuffer(ws[:4].cpu().numpy().tobytes(), np.uint32)[0])
+
+
+def _run_ws(spb, cuda, W, x, lab, **kw):
+    """Like _run but with an explicit workspace, also returning its error word."""
+    import torch
+    B, d = x.shape
+    f = lab.shape[1]
+    ws = spb.new_workspace(B, d, f, 0, cuda)
+    ws.zero_()
+    merge = torch.full((f,), -1, dtype=torch.int32, device=cuda)
+    count = torch.zeros(1, dtype=torch.int32, device=cuda)
+    out = spb.ffn_forward(*[_dev(w, cuda) for w in W], _dev(x, cuda), _dev(lab, cuda), merge_idx_out=merge,
+                          count_out=count, workspace=ws, **kw)
+    torch.cuda.synchronize()
+    return out.cpu().numpy(), merge.cpu().numpy(), int(count.cpu()[0]), _ws_error(ws)
+
+
+@pytest.mark.parametrize("B", [1, 5, 16, 33])
+def test_tensor_path_small_shapes(spb, cuda, oracle_mod, B):
+    rng = np.random.default_rng(200 + B)
+    d, f = 256, 1024
+    W = _layer(rng, d, f, 0.05)
+    x = rng.standard_normal((B, d)).astype(np.float32)
+    lab = (rng.random((B, f)) < 0.08).astype(np.float32)
+    out, merge, U, err = _run_ws(spb, cuda, W, x, lab, path=spb.PATH_TENSOR)
+    assert err == 0
+    m_ref, c_ref = oracle_mod.union(lab, B)
+    assert U == c_ref[0]
+    np.testing.assert_array_equal(merge[:U], m_ref[0, :U])
+    assert_close(out, oracle_mod.ffn(*W, x, lab))
+
+
+@pytest.mark.parametrize("B", [8, 16, 32])
+def test_tensor_path_7b_zipf(spb, cuda, oracle_mod, B):
+    """Config 2: 7B layer, Zipf(0.8) activity, 10% per token."""
+    rng = np.random.default_rng(B)
+    d, f = 4096, 11008
+    W = _layer(rng, d, f)
+    x = rng.standard_normal((B, d)).astype(np.float32)
+    lab = zipf_active_labels(B, f, 1101, seed=B)
+    out, merge, U, err = _run_ws(spb, cuda, W, x, lab, path=spb.PATH_TENSOR)
+    assert err == 0
+    ref_idx = np.nonzero((lab > 0).any(0))[0]
+    assert U == len(ref_idx)
+    np.testing.assert_array_equal(merge[:U], ref_idx)
+    assert_close(out, oracle_mod.ffn(*W, x, lab))
+
+
+@pytest.mark.parametrize("act", [0, 1])
+def test_tensor_path_union_semantics(spb, cuda, oracle_mod, act):
+    rng = np.random.default_rng(7)
+    B, d, f = 24, 1024, 2048
+    W = _layer(rng, d, f, 0.03)
+    x = rng.standard_normal((B, d)).astype(np.float32)
+    lab = zipf_active_labels(B, f, 205, seed=3)
+    out, _, _, err = _run_ws(spb, cuda, W, x, lab, path=spb.PATH_TENSOR, per_token_mask=False, act=act)
+    assert err == 0
+    assert_close(out, oracle_mod.ffn(*W, x, lab, per_token=False, act=act))
+
+
+def test_tensor_path_dense_and_large_batch(spb, cuda, oracle_mod):
+    """Every neuron active (a dense control) at B=128: split-K is off (T >= grid
+    would need f >= 19k), many tiles per chunk."""
+    rng = np.random.default_rng(9)
+    B, d, f = 128, 512, 1024
+    W = _layer(rng, d, f, 0.03)
+    x = rng.standard_normal((B, d)).astype(np.float32)
+    lab = np.ones((B, f), np.float32)
+    out, merge, U, err = _run_ws(spb, cuda, W, x, lab, path=spb.PATH_TENSOR)
+    assert err == 0 and U == f
+    assert_close(out, oracle_mod.ffn(*W, x, lab))
+
+
+def test_tensor_path_13b_b64(spb, cuda, oracle_mod):
+    """Config 3 layer shape: 13B, B=64, 8% activity."""
+    rng = np.random.default_rng(13)
+    B, d, f = 64, 5120, 13824
+    W = _layer(rng, d, f)
+    x = rng.standard_normal((B, d)).astype(np.float32)
+    lab = zipf_active_labels(B, f, 1106, seed=13)
+    out, merge, U, err = _run_ws(spb, cuda, W, x, lab, path=spb.PATH_TENSOR)
+    assert err == 0
+    assert U == int((lab > 0).any(0).sum())
+    assert_close(out, oracle_mod.ffn(*W, x, lab))
