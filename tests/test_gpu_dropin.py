@@ -139,18 +139,19 @@ def test_powerinfer_gemv_and_axpy(spb, cuda):
     idx = rng.standard_normal((B, f)).astype(np.float32)
     idx[:, ::5] = 0.0
     dst = torch.full((B, f), 1.0, device=cuda)
+    # keep every device tensor referenced until the kernels have run
+    wd_, yd_, idxd_ = _dev(w, cuda), _dev(y, cuda), _dev(idx, cuda)
     spb.dropin.fn("convert_mul_mat_batch_f16_cuda_sparse")(
-        _dev(w, cuda).data_ptr(), _dev(y, cuda).data_ptr(), dst.data_ptr(), d, f, B, f, _stream(), None,
-        _dev(idx, cuda).data_ptr())
+        wd_.data_ptr(), yd_.data_ptr(), dst.data_ptr(), d, f, B, f, _stream(), None, idxd_.data_ptr())
     want = 1.0 + np.where(idx > 0, y @ w.astype(np.float32).T, 0.0)
     torch.cuda.synchronize()
     assert_close(dst.cpu().numpy(), want)
     # axpy: W_down stored [f][d]; h [B][f]; token active when idx >= 0
     h = rng.standard_normal((B, f)).astype(np.float32)
     out = torch.zeros(B, d, device=cuda)
+    hd_ = _dev(h, cuda)
     spb.dropin.fn("convert_axpy_sparse_batch_f16_cuda")(
-        _dev(w, cuda).data_ptr(), _dev(h, cuda).data_ptr(), out.data_ptr(), d, f, f, B, _stream(), None,
-        _dev(idx, cuda).data_ptr())
+        wd_.data_ptr(), hd_.data_ptr(), out.data_ptr(), d, f, f, B, _stream(), None, idxd_.data_ptr())
     torch.cuda.synchronize()
     want = np.where(idx >= 0, h, 0.0) @ w.astype(np.float32)
     assert_close(out.cpu().numpy(), want)
@@ -179,7 +180,8 @@ def test_elementwise_and_dense(spb, cuda):
     am = (rng.standard_normal((M, K)) * 0.1).astype(np.float16)
     bm = rng.standard_normal((N, K)).astype(np.float32)
     c = torch.zeros(M, N, device=cuda)
-    spb.dropin.fn("gemm_cuda")(_dev(am, cuda).data_ptr(), _dev(bm, cuda).data_ptr(), c.data_ptr(), M, N, K, s)
+    amd, bmd = _dev(am, cuda), _dev(bm, cuda)
+    spb.dropin.fn("gemm_cuda")(amd.data_ptr(), bmd.data_ptr(), c.data_ptr(), M, N, K, s)
     torch.cuda.synchronize()
     assert_close(c.cpu().numpy(), am.astype(np.float32) @ bm.astype(np.float16).astype(np.float32).T)
 
@@ -194,8 +196,9 @@ def test_add_sparse(spb, cuda, oracle_mod):
     a = rng.standard_normal((B, f)).astype(np.float32)
     bias = rng.standard_normal(f).astype(np.float16)
     c = torch.zeros(B, f, device=cuda)
-    spb.dropin.fn("add_sparse_cuda")(_dev(a, cuda).data_ptr(), _dev(bias, cuda).data_ptr(), c.data_ptr(), f, B,
-                                     act.data_ptr(), _dev(merge, cuda).data_ptr(), _stream())
+    ad, biasd, merged = _dev(a, cuda), _dev(bias, cuda), _dev(merge, cuda)
+    spb.dropin.fn("add_sparse_cuda")(ad.data_ptr(), biasd.data_ptr(), c.data_ptr(), f, B, act.data_ptr(),
+                                     merged.data_ptr(), _stream())
     torch.cuda.synchronize()
     c = c.cpu().numpy()
     for t in range(B):
