@@ -102,6 +102,15 @@ int spb_ffn_forward(const void *w_gate, const void *w_up, const void *w_down, in
                     int32_t *merge_idx_out, int32_t *count_out, void *workspace, size_t workspace_bytes,
                     void *stream);
 
+/*
+ * Tracing: while enabled, tensor-path launches write per-CTA phase stamps
+ * (%globaltimer ns, 16 u64 slots per CTA: start, union scanned, gate/up
+ * issued, gate/up MMAs done, gate/up accumulators ready, h published, first
+ * down tile available, down issued, down accumulator ready, end) into
+ * `device_buffer` (at least grid * 16 u64 entries).  NULL disables.
+ */
+int spb_trace_enable(void *device_buffer, size_t slots);
+
 /* Kernel launches one spb_ffn_forward call makes for batch B and `path`. */
 int spb_ffn_launches(int B, int path);
 

@@ -14,7 +14,7 @@ import os
 from . import workload  # noqa: F401
 
 PKG = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(PKG, "libspbatch_b200.so")
+LIB_PATH = os.environ.get("SPB_LIB") or os.path.join(PKG, "libspbatch_b200.so")
 
 SPB_OK = 0
 W_F16, W_Q8_0, W_Q4_0 = 0, 1, 2
@@ -43,6 +43,7 @@ def lib() -> C.CDLL:
         L.spb_union.argtypes = [P, I, I, I, P, P, P, P, Z, P]
         L.spb_ffn_forward.argtypes = [P, P, P, I, P, P, I, I, I, I, I, I, P, P, P, P, Z, P]
         L.spb_ffn_launches.argtypes = [I, I]
+        L.spb_trace_enable.argtypes = [P, Z]
         _lib = L
     return _lib
 
@@ -76,7 +77,7 @@ def workspace_bytes(B: int, d: int, f: int, group: int = 0) -> int:
 
 def new_workspace(B: int, d: int, f: int, group: int = 0, device=None):
     import torch
-    return torch.empty(workspace_bytes(B, d, f, group), dtype=torch.uint8, device=device or "cuda")
+    return torch.zeros(workspace_bytes(B, d, f, group), dtype=torch.uint8, device=device or "cuda")
 
 
 def union(idx, group: int = 0, workspace=None, stream=None):

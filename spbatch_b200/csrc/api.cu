@@ -59,6 +59,15 @@ int ensure_smem(const void *kernel, size_t bytes) {
 
 constexpr int kGemvMaxBatch = 4;
 
+static std::mutex g_trace_mu;
+static void *g_trace_buf = nullptr;
+static size_t g_trace_slots = 0;
+
+void *trace_buffer(size_t slots) {
+    std::lock_guard<std::mutex> lk(g_trace_mu);
+    return g_trace_buf && slots <= g_trace_slots ? g_trace_buf : nullptr;
+}
+
 static bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 }  // namespace spb
@@ -181,6 +190,13 @@ int spb_ffn_forward(const void *w_gate, const void *w_up, const void *w_down, in
     a.count = count;
     a.out = out;
     return launch_fused_gemv(a, st);
+}
+
+int spb_trace_enable(void *device_buffer, size_t slots) {
+    std::lock_guard<std::mutex> lk(g_trace_mu);
+    g_trace_buf = device_buffer;
+    g_trace_slots = device_buffer ? slots : 0;
+    return SPB_OK;
 }
 
 int spb_ffn_launches(int B, int path) {

@@ -23,6 +23,9 @@ int num_sms();
 // and only when a larger size is requested, so calls made while a stream is
 // being captured into a CUDA graph do not repeat the attribute update.
 int ensure_smem(const void *kernel, size_t bytes);
+// Device buffer for per-CTA phase timestamps when tracing is enabled on the
+// current device and large enough for `slots` u64 entries; otherwise null.
+void *trace_buffer(size_t slots);
 
 #define SPB_CUDA_TRY(call)                                       \
     do {                                                         \
