@@ -10,8 +10,14 @@
 //                  K-slice of d.  Each ring stage holds one matrix's gathered
 //                  rows for nkb 64-wide K blocks (a contiguous 128*nkb-byte run
 //                  per row: DRAM efficiency of a row gather grows with the run
-//                  length) plus the matching fp16 activations, copied with
-//                  cp.async into the 128-byte-swizzled K-major layout.  Gate
+//                  length) plus the matching fp16 activations.  The gathered
+//                  rows arrive by cp.async (a warp copies one row's whole run
+//                  per instruction, so DRAM sees runs, not scattered lines),
+//                  the activations by 2D TMA tiles, all in the 128-byte-
+//                  swizzled K-major layout the MMA reads.  A stage's barrier
+//                  completes on the producers' cp.async arrivals plus the TMA
+//                  transaction bytes, so no producer waits on its own copies.
+//                  Gate
 //                  and up stages alternate; one thread issues
 //                  tcgen05.mma.kind::f16 M=128 x N=Np x K=16 into two TMEM
 //                  accumulators.  When several CTAs split a tile's K range,
@@ -25,29 +31,40 @@
 //                  a contiguous 512-byte run) are the MN-major A operand, h the
 //                  K-major B operand; out^T[2 x 128 x Np] accumulates in TMEM
 //                  and is added into the pre-zeroed output with fp32
-//                  reductions.  The W_down copies do not depend on h, so they
-//                  are issued before the h tile's ready flag is checked.
+//                  reductions.  Before its first stage each producer waits for
+//                  the ready flags of every gate/up tile the chunk reads.
 //
 // Warp roles (288 threads): warps 0-3 epilogue (TMEM lanes 0-127), warps 4-7
-// cp.async producers, warp 8 TMEM allocator + MMA issuer.  Every wait is
-// bounded (2 s of %globaltimer); on timeout the kernel records an error code in
-// the workspace and unwinds instead of hanging.
+// producers (cp.async + TMA), warp 8 TMEM allocator + MMA issuer.  Waiting
+// threads sleep on the mbarrier (try_wait with a suspend hint) instead of
+// spinning, which would steal shared-memory bandwidth from the producers.
+// Every wait is bounded (2 s of %globaltimer); on timeout the kernel records an
+// error code in the workspace and unwinds instead of hanging.
 #include "spb_internal.h"
 #include "spb_scan.cuh"
 #include "tc_ptx.cuh"
 
+#include <cuda.h>
+
 #include <algorithm>
 #include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
 
 namespace spb {
 
 using namespace ptx;
 
 constexpr int kTcThreads = 288;
+constexpr int kProducerWarp0 = 4;  // warps 4..7
+constexpr int kMmaWarp = 8;
 constexpr int kTileM = 128;          // neurons per gate/up tile, rows per MMA
 constexpr int kDnCols = 256;         // output columns per down item (two M=128 tiles)
 constexpr uint32_t kATile = 16384;   // 128 rows x 128 bytes (one 64-wide K block)
 constexpr int kMaxStages = 8;
+constexpr int kMaxGuUnits = 4;       // gate/up units per CTA the shared id table holds
 constexpr uint64_t kTimeoutNs = 2000000000ull;
 
 enum : uint32_t { kErrTimeoutFull = 1, kErrTimeoutEmpty = 2, kErrTimeoutAcc = 3, kErrTimeoutFlag = 4 };
@@ -70,7 +87,6 @@ struct Plan {
 
 struct TcArgs {
     const __half *wg, *wu, *wd;  // [f][d]
-    const __half *x16;           // [Np][d]
     __half *h16;                 // [Np][fpad]
     const uint32_t *seg_bits;    // [W]
     const uint32_t *tok_bits;    // [B][W]
@@ -81,40 +97,56 @@ struct TcArgs {
     uint32_t *tile_cnt;          // [Tmax], zero on entry
     uint32_t *tile_ready;        // [Tmax], zero on entry
     uint32_t *err;
-    unsigned long long *trace;   // [grid][kTraceSlots] %globaltimer stamps, or null
+    unsigned long long *trace;   // stamps, or null
     int B, Np, d, f, fpad, W, act, per_token;
     int P;                       // ring stages
     int nkb;                     // 64-wide K blocks per gate/up stage (row run = 128 * nkb bytes)
     int ns;                      // neurons per down stage (64 or 128)
-    int max_chunk;               // capacity of the shared down-unit id list
+    int debug;                   // profiling knobs (SPB_TC_DEBUG): 1 no MMAs, 2 no weight copies
+    int force_sk;                // profiling knob (SPB_TC_SK): K-split per tile, 0 = automatic
     uint32_t stage_bytes;
+};
+
+// TMA descriptors of the activations and of h (box 64 x Np, 128-byte swizzle).
+struct TcMaps {
+    CUtensorMap x, h;
 };
 
 // Phase stamps written when tracing is enabled (spb_trace_enable).
 enum TraceSlot {
     kTrStart = 0,        // after the dependency wait
-    kTrScanned = 1,      // union scanned, plan known
+    kTrScanned = 1,      // union scanned, ids emitted
     kTrGuIssued = 2,     // producers: last gate/up stage issued
     kTrGuMmaDone = 3,    // MMA: last gate/up stage issued + committed
     kTrGuAcc = 4,        // epilogue: gate/up accumulators ready
     kTrGuPublished = 5,  // epilogue: h written / partial handed off
-    kTrFirstFlag = 6,    // producers: first down-chunk h tile available
+    kTrFirstFlag = 6,    // producers: every h tile of the down chunk available
     kTrDnIssued = 7,     // producers: last down stage issued
     kTrDnAcc = 8,        // epilogue: last down accumulator ready
     kTrEnd = 9,          // before TMEM release
 };
 constexpr int kTraceSlots = 16;
+// Per-stage stamps of CTA 0: [stage][4] = producer past its empty wait,
+// producer done issuing, (unused), MMA thread sees the stage full.
+constexpr int kStageTraceBase = 160 * kTraceSlots;
+constexpr int kStageTraceMax = 256;
 
 __device__ __forceinline__ void stamp(const TcArgs &a, int slot) {
     if (a.trace) a.trace[(size_t)blockIdx.x * kTraceSlots + slot] = globaltimer();
 }
 
-__device__ __forceinline__ Plan make_plan(int U, int d, int nkb, int grid) {
+__device__ __forceinline__ void stage_stamp(const TcArgs &a, int stage, int what) {
+    if (a.trace && blockIdx.x == 0 && stage < kStageTraceMax)
+        a.trace[kStageTraceBase + stage * 4 + what] = globaltimer();
+}
+
+__device__ __forceinline__ Plan make_plan(int U, int d, int nkb, int grid, int force_sk) {
     Plan p;
     p.U = U;
     p.T = (U + kTileM - 1) / kTileM;
     p.KG = d / (64 * nkb);
     p.Sk = p.T ? max(1, min(min(8, p.KG), grid / p.T)) : 1;
+    if (force_sk > 0 && p.T) p.Sk = max(1, min(min(force_sk, p.KG), kMaxGuUnits * grid / p.T));
     p.ngu = p.T * p.Sk;
     p.MT = d / kDnCols;
     p.KC = p.T ? max(1, min(p.T, grid / p.MT)) : 0;
@@ -129,12 +161,16 @@ struct Unit {
     int stages;
 };
 
+__device__ __forceinline__ int num_gu_units(const Plan &p, int c, int grid) {
+    return p.ngu > c ? (p.ngu - c + grid - 1) / grid : 0;
+}
+
 // The u-th unit of CTA c: gate/up items c, c+grid, ... then its down item
 // (there is at most one: ndn <= grid).
 __device__ __forceinline__ Unit unit_of(const Plan &p, int c, int grid, int u, int ns) {
     Unit x{};
     x.kind = -1;
-    const int n_gu = p.ngu > c ? (p.ngu - c + grid - 1) / grid : 0;
+    const int n_gu = num_gu_units(p, c, grid);
     if (u < n_gu) {
         const int g = c + u * grid;
         const int ks = g % p.Sk;
@@ -156,20 +192,23 @@ __device__ __forceinline__ Unit unit_of(const Plan &p, int c, int grid, int u, i
     return x;
 }
 
-__device__ __forceinline__ int num_units(const Plan &p, int c, int grid) {
-    const int a = p.ngu > c ? (p.ngu - c + grid - 1) / grid : 0;
-    return a + (c < p.ndn ? 1 : 0);
-}
-
-// Neuron id at position pos of the ascending union list; bits and their
-// exclusive popcount scan are in shared memory.
-__device__ __forceinline__ int id_at(const uint32_t *bits, const int *prefix, int W, int pos) {
-    int lo = 0, hi = W - 1;  // last word with prefix[w] <= pos
-    while (lo < hi) {
-        const int mid = (lo + hi + 1) >> 1;
-        if (prefix[mid] <= pos) lo = mid; else hi = mid - 1;
+// Writes the neuron ids of union positions [P0, P1) to out[p - P0] (the whole
+// block cooperates, one 32-neuron word per thread); out[i] for
+// P1 - P0 <= i < n is set to `fill`.
+__device__ __forceinline__ void emit_ids(const uint32_t *bits, const int *prefix, int W, int P0, int P1, int n,
+                                         int fill, int *out) {
+    for (int i = max(P1 - P0, 0) + (int)threadIdx.x; i < n; i += blockDim.x) out[i] = fill;
+    for (int w = threadIdx.x; w < W; w += blockDim.x) {
+        int p = prefix[w];
+        if (prefix[w + 1] <= P0 || p >= P1) continue;
+        uint32_t word = bits[w];
+        while (word) {
+            const int b = __ffs(word) - 1;
+            word &= word - 1;
+            if (p >= P0 && p < P1) out[p - P0] = w * 32 + b;
+            ++p;
+        }
     }
-    return lo * 32 + (int)__fns(bits[lo], 0, pos - prefix[lo] + 1);
 }
 
 __device__ __forceinline__ void raise_error(uint32_t *err, TcCtl *ctl, uint32_t code) {
@@ -177,18 +216,33 @@ __device__ __forceinline__ void raise_error(uint32_t *err, TcCtl *ctl, uint32_t 
     ctl->abort = 1;
 }
 
-// Bounded mbarrier wait; false on timeout or abort.
-__device__ __forceinline__ bool wait_bar(uint64_t *bar, uint32_t parity, TcCtl *ctl, uint32_t *err, uint32_t code) {
-    for (int i = 0; i < 4096; ++i)
-        if (mbar_test(bar, parity)) return true;
+// Bounded mbarrier wait; false on timeout or abort.  `hint_ns` is how long a
+// waiting thread may sleep between checks (it wakes on completion).
+__device__ __forceinline__ bool wait_bar(uint64_t *bar, uint32_t parity, TcCtl *ctl, uint32_t *err, uint32_t code,
+                                         uint32_t hint_ns) {
+    if (mbar_test(bar, parity)) return true;
     const uint64_t t0 = globaltimer();
-    while (!mbar_test(bar, parity)) {
+    while (!mbar_test_sleep(bar, parity, hint_ns)) {
         if (ctl->abort) return false;
         if (globaltimer() - t0 > kTimeoutNs) {
             raise_error(err, ctl, code);
             return false;
         }
-        __nanosleep(64);
+    }
+    return true;
+}
+
+// Bounded wait for a gate/up tile's ready flag.
+__device__ __forceinline__ bool wait_flag(const uint32_t *flag, TcCtl *ctl, uint32_t *err) {
+    if (ld_acquire_u32(flag) != 0) return true;
+    const uint64_t t0 = globaltimer();
+    while (ld_acquire_u32(flag) == 0) {
+        if (ctl->abort) return false;
+        if (globaltimer() - t0 > kTimeoutNs) {
+            raise_error(err, ctl, kErrTimeoutFlag);
+            return false;
+        }
+        __nanosleep(256);
     }
     return true;
 }
@@ -198,23 +252,25 @@ __device__ __forceinline__ float act_h(float g, float u, int act) {
     return act == SPB_ACT_RELU_RELU_MUL ? g * fmaxf(u, 0.0f) : g * u;
 }
 
-__global__ void __launch_bounds__(kTcThreads, 1) ffn_tc_kernel(const TcArgs a) {
+__global__ void __launch_bounds__(kTcThreads, 1)
+ffn_tc_kernel(const __grid_constant__ TcMaps maps, const TcArgs a) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int P = a.P, W = a.W, Np = a.Np, nkb = a.nkb, ns = a.ns;
     uint8_t *ring = smem;
     TcCtl *ctl = reinterpret_cast<TcCtl *>(ring + (size_t)P * a.stage_bytes);
-    int *prefix = reinterpret_cast<int *>(ctl + 1);    // [W + 1]
-    int *wtot = prefix + W + 1;                         // [64]
+    int *prefix = reinterpret_cast<int *>(ctl + 1);           // [W + 1]
+    int *wtot = prefix + W + 1;                                // [64]
     uint32_t *bits = reinterpret_cast<uint32_t *>(wtot + 64);  // [W]
-    uint16_t *dn_ids = reinterpret_cast<uint16_t *>(bits + W);  // [max_chunk]
+    int *gu_ids = reinterpret_cast<int *>(bits + W);           // [kMaxGuUnits][128]
+    int *dn_ids = gu_ids + kMaxGuUnits * kTileM;               // [max_chunk]
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t ncols = Np * 2 <= 32 ? 32 : (Np * 2 <= 64 ? 64 : (Np * 2 <= 128 ? 128 : (Np * 2 <= 256 ? 256 : 512)));
 
     if (tid == 0) {
         for (int i = 0; i < P; ++i) {
-            mbar_init(&ctl->full[i], 128);
+            mbar_init(&ctl->full[i], 129);  // 128 producer cp.async arrivals + 1 TMA expect_tx arrival
             mbar_init(&ctl->empty[i], 1);
         }
         mbar_init(&ctl->acc_full, 1);
@@ -222,7 +278,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) ffn_tc_kernel(const TcArgs a) {
         ctl->abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    if (warp == 8) tmem_alloc(&ctl->tmem_base, ncols);
+    if (warp == kMmaWarp) tmem_alloc(&ctl->tmem_base, ncols);
 
     // Inputs written by the union launch become visible here.
     grid_dependency_wait();
@@ -231,165 +287,129 @@ __global__ void __launch_bounds__(kTcThreads, 1) ffn_tc_kernel(const TcArgs a) {
     __syncthreads();
     scan_popc(bits, W, prefix, wtot);  // ends with __syncthreads
     const int grid = gridDim.x, c = blockIdx.x;
-    const Plan pl = make_plan(prefix[W], a.d, nkb, grid);
+    const Plan pl = make_plan(prefix[W], a.d, nkb, grid, a.force_sk);
     if (c == 0 && tid == 0) *a.count_out = pl.U;
-    const int nunits = num_units(pl, c, grid);
-    // ids of this CTA's down chunk, shared by its producers
-    const Unit dn = unit_of(pl, c, grid, nunits - 1, ns);
-    if (dn.kind == 1) {
-        const int n = dn.stages * ns;
-        for (int i = dn.P1 - dn.P0 + tid; i < n; i += kTcThreads) dn_ids[i] = 0xFFFF;
-        for (int w = tid; w < W; w += kTcThreads) {  // word-parallel emission of [P0, P1)
-            int p = prefix[w];
-            if (prefix[w + 1] <= dn.P0 || p >= dn.P1) continue;
-            uint32_t word = bits[w];
-            while (word) {
-                const int b = __ffs(word) - 1;
-                word &= word - 1;
-                if (p >= dn.P0 && p < dn.P1) dn_ids[p - dn.P0] = (uint16_t)(w * 32 + b);
-                ++p;
-            }
-        }
+    const int n_gu = min(num_gu_units(pl, c, grid), kMaxGuUnits);
+    const int nunits = n_gu + (c < pl.ndn ? 1 : 0);
+    // neuron ids of this CTA's tiles and down chunk; a.f (out of range) marks
+    // padding rows, which are zero-filled
+    for (int u = 0; u < n_gu; ++u) {
+        const Unit un = unit_of(pl, c, grid, u, ns);
+        emit_ids(bits, prefix, W, un.tile * kTileM, min(pl.U, un.tile * kTileM + kTileM), kTileM, a.f,
+                 gu_ids + u * kTileM);
     }
+    const Unit dn = unit_of(pl, c, grid, n_gu, ns);
+    if (dn.kind == 1) emit_ids(bits, prefix, W, dn.P0, dn.P1, dn.stages * ns, a.f, dn_ids);
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = ctl->tmem_base;
     if (tid == 0) stamp(a, kTrScanned);
 
-    if (warp >= 4 && warp < 8) {
+    if (warp >= kProducerWarp0 && warp < kProducerWarp0 + 4) {
         // ------------------------------------------------------------ producers
-        const int pt = tid - 128;
-        const int lag = P - 1;
-        const int cpr = nkb * 8;  // 16-byte chunks per row per gate/up stage
-        int s = 0;                // stages committed
-        int arrived = 0;          // stages whose full barrier this thread has arrived on
-        int known_ready = -1;     // highest tile index whose ready flag this thread has seen
-        // Arrive on every committed stage.  Must run before any wait on another
-        // tile's ready flag: the stages still held back by the lag may be the
-        // ones this CTA's own gate/up epilogue (and so some flag) depends on.
-        auto flush = [&]() {
-            cp_async_wait(0);
-            fence_proxy_async_smem();
-            for (; arrived < s; ++arrived) mbar_arrive(&ctl->full[arrived % P]);
-        };
-        for (int u = 0; u < nunits && !ctl->abort; ++u) {
+        const int pt = tid - kProducerWarp0 * 32, pw = pt >> 5;
+        const bool leader = pt == 0;
+        const bool copy_w = !(a.debug & 2);
+        int s = 0;
+        for (int u = 0; u < nunits; ++u) {
             const Unit un = unit_of(pl, c, grid, u, ns);
-            // gate/up: this thread copies chunk (pt % cpr) of rows i * (128 / cpr) + pt / cpr
-            int rid[32];
-            if (un.kind == 0) {
-                const int rstep = 128 / cpr;
-#pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    if (i < cpr) {
-                        const int pos = un.tile * kTileM + i * rstep + pt / cpr;
-                        rid[i] = pos < pl.U ? id_at(bits, prefix, W, pos) : -1;
-                    }
-                }
+            bool ok = true;
+            if (un.kind == 1 && un.stages > 0) {
+                // Every gate/up tile this chunk reads h from must be published.
+                // Each producer checks all of them itself: no barrier that a
+                // thread leaving on a timeout could strand the others at.
+                const int t0 = un.P0 / kTileM, t1 = (un.P0 + un.stages * ns - 1) / kTileM;
+                for (int t = t0; t <= t1 && ok; ++t) ok = wait_flag(a.tile_ready + t, ctl, a.err);
+                if (!ok) break;
+                if (leader) stamp(a, kTrFirstFlag);
             }
+            // CTAs sharing a K range start at different K groups: rows are 8 KB
+            // apart, so CTAs stepping through the same column window in lock
+            // step would all hit the same few DRAM channels.
+            const int nk = un.kind == 0 ? un.kg1 - un.kg0 : 1;
+            const int rot = un.kind == 0 && nk > 0 ? (un.tile % nk) : 0;
             for (int st = 0; st < un.stages; ++st, ++s) {
                 const int slot = s % P, round = s / P;
-                if (round > 0 && !wait_bar(&ctl->empty[slot], (round - 1) & 1, ctl, a.err, kErrTimeoutEmpty)) break;
+                ok = round == 0 || wait_bar(&ctl->empty[slot], (round - 1) & 1, ctl, a.err, kErrTimeoutEmpty, 1000);
+                if (!ok) break;
+                uint64_t *bar = &ctl->full[slot];
                 const uint32_t sbase = smem_u32(ring + (size_t)slot * a.stage_bytes);
+                if (leader) stage_stamp(a, s, 0);
                 if (un.kind == 0) {
-                    const int kg = un.kg0 + (st >> 1);
-                    const __half *w = (st & 1) ? a.wu : a.wg;
-                    const int kbase = kg * 64 * nkb;
-                    const int ch = pt % cpr, kbl = ch >> 3, cc = ch & 7;
-                    const int rstep = 128 / cpr;
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) {
-                        if (i < cpr) {
-                            const int r = i * rstep + pt / cpr;
-                            const int j = rid[i];
-                            cp_async16(sbase + kbl * kATile + r * 128 + ((cc ^ (r & 7)) << 4),
-                                       w + (int64_t)(j < 0 ? 0 : j) * a.d + kbase + ch * 8, j < 0 ? 0u : 16u);
-                        }
+                    const int kbase = (un.kg0 + ((st >> 1) + rot) % nk) * 64 * nkb;
+                    if (leader) {  // activations: nkb TMA tiles of 64 columns x Np rows
+                        mbar_arrive_expect_tx(bar, (uint32_t)nkb * Np * 128);
+                        for (int kbl = 0; kbl < nkb; ++kbl)
+                            tma_load_2d(sbase + nkb * kATile + kbl * Np * 128, &maps.x, bar, kbase + kbl * 64, 0);
                     }
-                    const uint32_t xoff = nkb * kATile;
-                    for (int q = pt; q < Np * cpr; q += 128) {
-                        const int r = q / cpr, xc = q % cpr;
-                        cp_async16(sbase + xoff + (xc >> 3) * (Np * 128) + r * 128 + (((xc & 7) ^ (r & 7)) << 4),
-                                   a.x16 + (int64_t)r * a.d + kbase + xc * 8, 16u);
+                    // weights: 128 rows x (nkb x 128 B); each warp instruction copies whole row runs
+                    const __half *w = ((st & 1) ? a.wu : a.wg) + kbase;
+                    const int cpr = nkb * 8;    // 16-byte chunks per row run
+                    const int rpw = 32 / cpr;   // rows per warp instruction
+                    const int ch = lane & (cpr - 1), kbl = ch >> 3, cc = ch & 7;
+                    if (copy_w) {
+                        const __half *wl = w + ch * 8;
+                        const uint32_t dl = sbase + kbl * kATile + (uint32_t)cc * 16;
+                        for (int r = pw * rpw + lane / cpr; r < 128; r += 4 * rpw) {
+                            const int j = gu_ids[u * kTileM + r];
+                            // padding rows past the union copy row 0: the epilogue
+                            // zeroes h for them, so their products are never used
+                            cp_async16_full((dl + r * 128) ^ ((uint32_t)(r & 7) << 4),
+                                            wl + (int64_t)(j < a.f ? j : 0) * a.d);
+                        }
                     }
                 } else {
                     const int p0s = un.P0 + st * ns;
+                    if (leader) {  // h: ns/64 TMA tiles of 64 neurons x Np tokens
+                        mbar_arrive_expect_tx(bar, (uint32_t)(ns / 64) * Np * 128);
+                        for (int kbl = 0; kbl < ns / 64; ++kbl)
+                            tma_load_2d(sbase + (uint32_t)ns * 512 + kbl * Np * 128, &maps.h, bar, p0s + kbl * 64, 0);
+                    }
+                    // W_down rows as the MN-major operand: ns neurons x 256 columns (32 chunks), one row per warp
                     const int m0 = un.mt * kDnCols;
                     const uint32_t lbo = (uint32_t)(ns / 8) * 1024;
-                    // W_down rows, MN-major: ns neurons x 32 chunks (256 columns); lane = chunk
-                    const int ch = pt & 31, mt2 = ch >> 4, mh = (ch >> 3) & 1, cc = ch & 7;
-                    for (int kk = pt >> 5; kk < ns; kk += 4) {
-                        const uint16_t id = dn_ids[p0s - un.P0 + kk];
-                        const int kg = kk >> 3, kr = kk & 7;
-                        const uint32_t dst = mt2 * 2 * lbo + mh * lbo + kg * 1024 + kr * 128 + ((cc ^ kr) << 4);
-                        cp_async16(sbase + dst, a.wd + (int64_t)(id == 0xFFFF ? 0 : id) * a.d + m0 + ch * 8,
-                                   id == 0xFFFF ? 0u : 16u);
-                    }
-                    // h of these neurons: wait for their gate/up tile to be published
-                    const int tile = p0s / kTileM;
-                    if (tile > known_ready) {
-                        const uint32_t *flag = a.tile_ready + tile;
-                        bool ok = ld_acquire_u32(flag) != 0;
-                        if (!ok) {
-                            cp_async_commit();  // the W_down copies above, as their own group
-                            flush();
-                            const uint64_t t0 = globaltimer();
-                            while (!(ok = ld_acquire_u32(flag) != 0)) {
-                                if (ctl->abort) break;
-                                if (globaltimer() - t0 > kTimeoutNs) {
-                                    raise_error(a.err, ctl, kErrTimeoutFlag);
-                                    break;
-                                }
-                                __nanosleep(128);
-                            }
+                    const int mb = lane >> 3, cc = lane & 7;
+                    if (copy_w) {
+                        for (int kk = pw; kk < ns; kk += 4) {
+                            const int j = dn_ids[(p0s - un.P0) + kk];
+                            const int kg = kk >> 3, kr = kk & 7;
+                            cp_async16(sbase + mb * lbo + kg * 1024 + kr * 128 + ((cc ^ kr) << 4),
+                                       a.wd + (int64_t)(j < a.f ? j : 0) * a.d + m0 + lane * 8, j < a.f ? 16u : 0u);
                         }
-                        if (!ok) break;
-                        known_ready = tile;
-                        if (pt == 0 && st == 0) stamp(a, kTrFirstFlag);
-                    }
-                    const uint32_t hoff = (uint32_t)ns * 512;
-                    const int hcpr = ns / 8;
-                    for (int q = pt; q < Np * hcpr; q += 128) {
-                        const int t = q / hcpr, hc = q % hcpr;
-                        cp_async16(sbase + hoff + (hc >> 3) * (Np * 128) + t * 128 + (((hc & 7) ^ (t & 7)) << 4),
-                                   a.h16 + (int64_t)t * a.fpad + p0s + hc * 8, 16u);
                     }
                 }
-                cp_async_commit();
-                // keep `lag` stages of copies in flight; a stage's groups
-                // complete in order, so once at most `lag` groups are pending
-                // the oldest unarrived stage has landed
-                if (s + 1 - arrived > lag) {
-                    cp_async_wait(lag);
-                    fence_proxy_async_smem();
-                    mbar_arrive(&ctl->full[arrived % P]);
-                    ++arrived;
-                }
+                cp_async_mbar_arrive(bar);
+                if (leader) stage_stamp(a, s, 1);
             }
-            if (pt == 0) stamp(a, un.kind == 0 ? kTrGuIssued : kTrDnIssued);
-            if (ctl->abort) break;
+            if (!ok) break;
+            if (leader) stamp(a, un.kind == 0 ? kTrGuIssued : kTrDnIssued);
         }
-        flush();  // release the stages still in flight
-    } else if (warp == 8) {
+    } else if (warp == kMmaWarp) {
         // ------------------------------------------------------------ MMA issuer
         if (lane == 0) {
             const uint32_t id_gu = idesc_f16_f32(kTileM, Np, false, false);
             const uint32_t id_dn = idesc_f16_f32(kTileM, Np, true, false);
             const uint32_t lbo = (uint32_t)(ns / 8) * 1024;
+            const bool do_mma = !(a.debug & 1);
             int s = 0;
             for (int u = 0; u < nunits && !ctl->abort; ++u) {
                 const Unit un = unit_of(pl, c, grid, u, ns);
-                if (u > 0 && !wait_bar(&ctl->acc_empty, (u - 1) & 1, ctl, a.err, kErrTimeoutAcc)) break;
+                if (u > 0 && !wait_bar(&ctl->acc_empty, (u - 1) & 1, ctl, a.err, kErrTimeoutAcc, 2000)) break;
                 tc_fence_after();
                 bool ok = true;
                 for (int st = 0; st < un.stages; ++st, ++s) {
                     const int slot = s % P, round = s / P;
-                    if (!wait_bar(&ctl->full[slot], round & 1, ctl, a.err, kErrTimeoutFull)) {
+                    if (!wait_bar(&ctl->full[slot], round & 1, ctl, a.err, kErrTimeoutFull, 1000)) {
                         ok = false;
                         break;
                     }
+                    stage_stamp(a, s, 3);
+                    // the producers' cp.async data were written through the
+                    // generic proxy; make them visible to the MMA's async proxy
+                    fence_proxy_async_smem();
                     tc_fence_after();
                     const uint32_t sbase = smem_u32(ring + (size_t)slot * a.stage_bytes);
-                    if (un.kind == 0) {
+                    if (do_mma && un.kind == 0) {
                         const uint32_t dcol = tmem + (st & 1) * Np;  // gate or up accumulator
                         const uint32_t xoff = nkb * kATile;
                         for (int kbl = 0; kbl < nkb; ++kbl) {
@@ -400,7 +420,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) ffn_tc_kernel(const TcArgs a) {
                                 mma_f16(dcol, ad, bd, id_gu, (st > 1 || kbl > 0 || k4 > 0) ? 1u : 0u);
                             }
                         }
-                    } else {
+                    } else if (do_mma) {
                         const uint32_t hoff = (uint32_t)ns * 512;
                         for (int kbl = 0; kbl < ns / 64; ++kbl) {
 #pragma unroll
@@ -430,14 +450,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) ffn_tc_kernel(const TcArgs a) {
         const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
         for (int u = 0; u < nunits; ++u) {
             const Unit un = unit_of(pl, c, grid, u, ns);
-            const bool ok = wait_bar(&ctl->acc_full, u & 1, ctl, a.err, kErrTimeoutAcc);
+            const bool ok = wait_bar(&ctl->acc_full, u & 1, ctl, a.err, kErrTimeoutAcc, 20000);
             if (!named_bar_and(2, 128, ok)) break;
             tc_fence_after();
             if (e == 0) stamp(a, un.kind == 0 ? kTrGuAcc : kTrDnAcc);
             if (un.kind == 0) {
                 const int pos = un.tile * kTileM + e;
                 const bool valid = pos < pl.U;
-                const int j = valid ? id_at(bits, prefix, W, pos) : 0;
+                const int j = valid ? gu_ids[u * kTileM + e] : 0;
                 const bool direct = pl.Sk == 1;
                 const uint32_t *mrow = a.tok_bits + (j >> 5);
                 float *part = a.partial + (size_t)(c + u * grid) * 2 * Np * kTileM;  // gate/up item index
@@ -539,16 +559,73 @@ __global__ void __launch_bounds__(kTcThreads, 1) ffn_tc_kernel(const TcArgs a) {
 
     __syncthreads();
     if (tid == 0) stamp(a, kTrEnd);
-    if (warp == 8) {
-        if (ctl->abort) __nanosleep(100000);  // let in-flight MMAs drain before freeing TMEM
+    if (warp == kMmaWarp) {
+        if (ctl->abort) __nanosleep(100000);  // let in-flight MMAs and copies drain before freeing TMEM
         tc_fence_after();
         tmem_dealloc(tmem, ncols);
     }
 }
 
 // ---------------------------------------------------------------------------------
-// Stage geometry: the largest row run (K blocks per gate/up stage) that still
-// leaves two ring stages; the down stage uses the same slot.
+// Tensor maps are encoded on the host once per (device, address, shape) and cached.
+namespace {
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+struct MapKey {
+    int dev;
+    const void *ptr;
+    uint64_t cols, rows;
+    uint32_t box_rows;
+    bool operator==(const MapKey &o) const {
+        return dev == o.dev && ptr == o.ptr && cols == o.cols && rows == o.rows && box_rows == o.box_rows;
+    }
+};
+
+// fp16 matrix [rows][cols] (row-major), box of 64 columns x box_rows rows,
+// 128-byte swizzle, out-of-range elements read as zero.
+int tensor_map(const void *ptr, uint64_t cols, uint64_t rows, uint32_t box_rows, CUtensorMap *out) {
+    static std::mutex mu;
+    static std::vector<std::pair<MapKey, CUtensorMap>> cache;
+    static EncodeTiledFn encode = nullptr;
+    int dev = 0;
+    SPB_CUDA_TRY(cudaGetDevice(&dev));
+    const MapKey key{dev, ptr, cols, rows, box_rows};
+    std::lock_guard<std::mutex> lk(mu);
+    for (auto &e : cache)
+        if (e.first == key) {
+            *out = e.second;
+            return SPB_OK;
+        }
+    if (!encode) {
+        void *fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        SPB_CUDA_TRY(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q));
+        if (!fn || q != cudaDriverEntryPointSuccess) return fail(SPB_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+        encode = reinterpret_cast<EncodeTiledFn>(fn);
+    }
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t strides[1] = {cols * 2};
+    const cuuint32_t box[2] = {64, box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    CUtensorMap m;
+    memset(&m, 0, sizeof(m));
+    const CUresult r = encode(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(ptr), dims, strides, box,
+                              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(SPB_ERR_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
+    if (cache.size() > 4096) cache.clear();
+    cache.push_back({key, m});
+    *out = m;
+    return SPB_OK;
+}
+
+}  // namespace
+
+// Stage geometry: the longest row run (K blocks per gate/up stage) that still
+// leaves `want` ring stages; the down stage uses the same slot.
 struct Geometry {
     int nkb, ns, P;
     uint32_t stage_bytes;
@@ -557,15 +634,13 @@ struct Geometry {
 
 static Geometry pick_geometry(int Np, int W, int max_chunk, int d) {
     const size_t fixed = sizeof(TcCtl) + sizeof(int) * (W + 1 + 64) + sizeof(uint32_t) * W +
-                         sizeof(uint16_t) * max_chunk + 1024 + 64;
+                         sizeof(int) * (kMaxGuUnits * kTileM + max_chunk) + 1024 + 64;
     const size_t budget = 227 * 1024;
     const char *env = getenv("SPB_TC_NKB");
     const int forced = env ? atoi(env) : 0;
     const char *envp = getenv("SPB_TC_MINP");
-    const int want_p = envp ? atoi(envp) : 4;
+    const int want_p = envp ? atoi(envp) : 2;
     Geometry best{0, 0, 0, 0, 0};
-    // Longest row run (nkb) that keeps at least want_p ring stages: the ring is
-    // what keeps enough bytes in flight per SM; fall back to any P >= 2.
     for (int pass = 0; pass < 2 && best.P == 0; ++pass) {
         for (int nkb = 4; nkb >= 1; --nkb) {
             if (forced && nkb != forced) continue;
@@ -575,6 +650,7 @@ static Geometry pick_geometry(int Np, int W, int max_chunk, int d) {
             if ((uint32_t)ns * 512 + 2u * Np * 128 > gu) ns = 64;
             const uint32_t dn = (uint32_t)ns * 512 + (uint32_t)(ns / 64) * Np * 128;
             const uint32_t stage = ((gu > dn ? gu : dn) + 1023) & ~1023u;
+            if (fixed + 2 * (size_t)stage > budget) continue;
             const int P = (int)std::min<size_t>((budget - fixed) / stage, kMaxStages);
             if (P >= (pass == 0 ? want_p : 2)) {
                 best = Geometry{nkb, ns, P, stage, fixed + (size_t)P * stage};
@@ -593,7 +669,6 @@ int launch_ffn_tc(const TcLaunch &L, cudaStream_t st) {
     a.wg = static_cast<const __half *>(L.wg);
     a.wu = static_cast<const __half *>(L.wu);
     a.wd = static_cast<const __half *>(L.wd);
-    a.x16 = L.x16;
     a.h16 = L.h16;
     a.seg_bits = L.seg_bits;
     a.tok_bits = L.tok_bits;
@@ -604,7 +679,7 @@ int launch_ffn_tc(const TcLaunch &L, cudaStream_t st) {
     a.tile_cnt = L.tile_cnt;
     a.tile_ready = L.tile_ready;
     a.err = L.err;
-    a.trace = static_cast<unsigned long long *>(trace_buffer((size_t)L.grid * kTraceSlots));
+    a.trace = static_cast<unsigned long long *>(trace_buffer((size_t)kStageTraceBase + kStageTraceMax * 4));
     a.B = L.B;
     a.Np = Np;
     a.d = L.d;
@@ -613,19 +688,26 @@ int launch_ffn_tc(const TcLaunch &L, cudaStream_t st) {
     a.W = words_of(L.f);
     a.act = L.act;
     a.per_token = L.per_token;
+    a.debug = getenv("SPB_TC_DEBUG") ? atoi(getenv("SPB_TC_DEBUG")) : 0;
+    a.force_sk = getenv("SPB_TC_SK") ? atoi(getenv("SPB_TC_SK")) : 0;
     // Longest down chunk: ceil(T / KC) tiles with KC = min(T, grid / MT).
     const int Tmax = (L.f + kTileM - 1) / kTileM;
     const int MT = L.d / kDnCols;
     const int KCmin = std::max(1, std::min(Tmax, L.grid / MT));
-    a.max_chunk = ((Tmax + KCmin - 1) / KCmin + 1) * kTileM;
-    const Geometry g = pick_geometry(Np, a.W, a.max_chunk, L.d);
+    const int max_chunk = ((Tmax + KCmin - 1) / KCmin + 1) * kTileM;
+    if ((Tmax + L.grid - 1) / L.grid > kMaxGuUnits) return fail(SPB_ERR_UNSUPPORTED, "tensor path: f too large");
+    const Geometry g = pick_geometry(Np, a.W, max_chunk, L.d);
     if (g.P < 2) return fail(SPB_ERR_UNSUPPORTED, "tensor path: shared memory too small for two stages");
-    if ((L.d / 64) % g.nkb) return fail(SPB_ERR_INVALID, "tensor path: d does not split into stage K blocks");
     a.P = g.P;
     a.nkb = g.nkb;
     a.ns = g.ns;
     a.stage_bytes = g.stage_bytes;
-    if (int rc = ensure_smem((const void *)ffn_tc_kernel, g.smem)) return rc;
+
+    TcMaps maps;
+    int rc;
+    if ((rc = tensor_map(L.x16, L.d, Np, Np, &maps.x))) return rc;
+    if ((rc = tensor_map(L.h16, L.fpad, Np, Np, &maps.h))) return rc;
+    if ((rc = ensure_smem((const void *)ffn_tc_kernel, g.smem))) return rc;
 
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(L.grid);
@@ -637,7 +719,7 @@ int launch_ffn_tc(const TcLaunch &L, cudaStream_t st) {
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    SPB_CUDA_TRY(cudaLaunchKernelEx(&cfg, ffn_tc_kernel, a));
+    SPB_CUDA_TRY(cudaLaunchKernelEx(&cfg, ffn_tc_kernel, maps, a));
     return SPB_OK;
 }
 

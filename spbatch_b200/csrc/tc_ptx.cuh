@@ -49,10 +49,45 @@ __device__ __forceinline__ bool mbar_test(uint64_t *bar, uint32_t parity) {
     return ok != 0;
 }
 
+// Like mbar_test, but a thread whose phase is not complete may sleep for up to
+// `hint_ns` (it wakes when the phase completes): long waits then cost no issue
+// slots or shared-memory bandwidth that the copying warps need.
+__device__ __forceinline__ bool mbar_test_sleep(uint64_t *bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+
+// Arrive on `bar` and raise its expected transaction count by `bytes`.
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile(
+        "{\n\t.reg .b64 st;\n\t"
+        "mbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(smem_u32(bar)),
+        "r"(bytes)
+        : "memory");
+}
+
 // ---- cp.async ---------------------------------------------------------------
 // 16-byte global -> shared copy; src_bytes = 0 zero-fills the destination.
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, uint32_t src_bytes) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+
+// Arrive on `bar` once every cp.async this thread issued so far has landed
+// (the arrival counts against the barrier's expected count).
+__device__ __forceinline__ void cp_async_mbar_arrive(uint64_t *bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// 16-byte global -> shared copy without the zero-fill operand.
+__device__ __forceinline__ void cp_async16_full(uint32_t dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
 }
 
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
@@ -104,6 +139,17 @@ __device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t *p) {
 
 __device__ __forceinline__ void st_release_u32(uint32_t *p, uint32_t v) {
     asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// ---- TMA ----------------------------------------------------------------------
+// 2D tile load of the tensor map's box at coordinates (c0 innermost, c1);
+// completion is signalled as transaction bytes on `bar`.
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const void *tmap, uint64_t *bar, int c0, int c1) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+        : "memory");
 }
 
 // ---- programmatic dependent launch -------------------------------------------
