@@ -103,6 +103,24 @@ int spb_ffn_forward(const void *w_gate, const void *w_up, const void *w_down, in
                     void *stream);
 
 /*
+ * Allocation-free variant of spb_union for callers that cannot allocate
+ * device memory (a framework allocator owns the device, a plug-in receives
+ * only its input and output buffers, or a latency-critical path must not call
+ * cudaMalloc).  It has no counterpart in the reference.  Same arguments and
+ * results as spb_union minus the workspace: its scratch (ceil(S*W/64)*64 + S + 1
+ * 32-bit words, S = segments, W = ceil(f/32)) lives in a 65536-word (256 KB)
+ * device array inside the library, held by every GPU that loads the library
+ * until the process exits.  Larger requests fail with SPB_ERR_UNSUPPORTED.
+ * The first call on a device looks up that array's device address, so make
+ * it before capturing a stream.  All calls share the array: calls that
+ * overlap on the GPU (different streams, or concurrent devices' threads
+ * using the same device) race; serialise them.  Every scratch word a call
+ * reads is written by that same call, so no clearing is needed between calls.
+ */
+int spb_union_static(const float *idx, int B, int f, int group, int32_t *merge_idx, int32_t *act_cum,
+                     uint32_t *tok_bits, void *stream);
+
+/*
  * Tracing: while enabled, tensor-path launches write per-CTA phase stamps
  * (%globaltimer ns, 16 u64 slots per CTA: start, union scanned, gate/up
  * issued, gate/up MMAs done, gate/up accumulators ready, h published, first

@@ -41,6 +41,7 @@ def lib() -> C.CDLL:
         L.spb_ffn_workspace_bytes.argtypes = [I, I, I, I]
         L.spb_ffn_workspace_bytes.restype = Z
         L.spb_union.argtypes = [P, I, I, I, P, P, P, P, Z, P]
+        L.spb_union_static.argtypes = [P, I, I, I, P, P, P, P]
         L.spb_ffn_forward.argtypes = [P, P, P, I, P, P, I, I, I, I, I, I, P, P, P, P, Z, P]
         L.spb_ffn_launches.argtypes = [I, I]
         L.spb_trace_enable.argtypes = [P, Z]

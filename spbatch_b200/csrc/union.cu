@@ -15,6 +15,10 @@
 //
 // The fused FFN path skips compact_kernel: its CTAs rebuild the slice of the
 // index list they own from the segment bits (spb_scan.cuh).
+#include <mutex>
+#include <string>
+#include <vector>
+
 #include "spb_internal.h"
 #include "spb_scan.cuh"
 
@@ -147,3 +151,71 @@ int launch_compact(const uint32_t *seg_bits, int S, int f, int32_t *merge_idx, i
 }
 
 }  // namespace spb
+
+// ---------------------------------------------------------------------------
+// Allocation-free union entry point.
+//
+// Some callers cannot allocate device memory at the point where they need
+// the union: code running inside a framework whose allocator owns the whole
+// device, plug-ins that are handed only input and output buffers, and
+// real-time paths that may not call cudaMalloc (it can synchronise the
+// device).  spb_union_static serves them with the same kernels as spb_union,
+// but its scratch -- the per-segment union bit words and the per-segment
+// counts -- lives in the fixed device array below instead of a caller
+// workspace.  The array is part of the library image: every GPU that loads
+// the library holds it (256 KB) until the process exits.
+namespace spb {
+namespace {
+
+constexpr int kUnionStaticWords = 1 << 16;  // 65536 u32 words = 256 KB
+
+static __device__ __align__(256) uint32_t g_union_static_scratch[kUnionStaticWords];
+
+// Device address of the array on the current device; looked up once per
+// device (host code must not use the symbol itself as a device pointer).
+int static_scratch_address(uint32_t **out) {
+    static std::mutex mu;
+    static std::vector<uint32_t *> addr;
+    int dev = 0;
+    SPB_CUDA_TRY(cudaGetDevice(&dev));
+    std::lock_guard<std::mutex> lk(mu);
+    if ((int)addr.size() <= dev) addr.resize(dev + 1, nullptr);
+    if (!addr[dev]) {
+        void *p = nullptr;
+        SPB_CUDA_TRY(cudaGetSymbolAddress(&p, g_union_static_scratch));
+        addr[dev] = static_cast<uint32_t *>(p);
+    }
+    *out = addr[dev];
+    return SPB_OK;
+}
+
+}  // namespace
+}  // namespace spb
+
+extern "C" int spb_union_static(const float *idx, int B, int f, int group, int32_t *merge_idx, int32_t *act_cum,
+                                uint32_t *tok_bits, void *stream) {
+    using namespace spb;
+    if (!idx || !merge_idx || !act_cum) return fail(SPB_ERR_INVALID, "spb_union_static: null pointer");
+    if (B <= 0 || f <= 0 || group < 0) return fail(SPB_ERR_INVALID, "spb_union_static: bad shape");
+    const int G = group == 0 ? B : group;
+    const int S = (B + G - 1) / G;
+    const int W = words_of(f);
+    // scratch: S*W union words, then S+1 counts (each region 64-word aligned)
+    const int64_t words_bits = ((int64_t)S * W + 63) / 64 * 64;
+    const int64_t need = words_bits + S + 1;
+    if (need > kUnionStaticWords)
+        return fail(SPB_ERR_UNSUPPORTED, "spb_union_static: segments x words (" + std::to_string(need) +
+                                             " words of scratch) exceed the fixed 65536-word scratch array; "
+                                             "use spb_union with a workspace");
+    uint32_t *scratch = nullptr;
+    if (int rc = static_scratch_address(&scratch)) return rc;
+    uint32_t *seg_bits = scratch;
+    int32_t *counts = reinterpret_cast<int32_t *>(scratch + words_bits);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    // Every segment word and count is rewritten by these launches, so nothing
+    // left in the array by an earlier call is read.
+    int rc = launch_union_bits(idx, B, f, G, tok_bits, seg_bits, PrepJobs{}, st);
+    if (rc) return rc;
+    return launch_compact(seg_bits, S, f, merge_idx, act_cum, counts, st);
+}
+
