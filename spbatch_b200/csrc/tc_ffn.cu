@@ -124,6 +124,10 @@ enum TraceSlot {
     kTrDnIssued = 7,     // producers: last down stage issued
     kTrDnAcc = 8,        // epilogue: last down accumulator ready
     kTrEnd = 9,          // before TMEM release
+    kTrBits = 10,        // union words copied to shared memory
+    kTrScan = 11,        // scan done
+    kTrGuIds = 12,       // gate/up tile ids emitted
+    kTrDnIds = 13,       // down chunk ids emitted
 };
 constexpr int kTraceSlots = 16;
 // Per-stage stamps of CTA 0: [stage][4] = producer past its empty wait,
@@ -285,7 +289,9 @@ ffn_tc_kernel(const __grid_constant__ TcMaps maps, const TcArgs a) {
     if (tid == 0) stamp(a, kTrStart);
     for (int w = tid; w < W; w += kTcThreads) bits[w] = a.seg_bits[w];
     __syncthreads();
+    if (tid == 0) stamp(a, kTrBits);
     scan_popc(bits, W, prefix, wtot);  // ends with __syncthreads
+    if (tid == 0) stamp(a, kTrScan);
     const int grid = gridDim.x, c = blockIdx.x;
     const Plan pl = make_plan(prefix[W], a.d, nkb, grid, a.force_sk);
     if (c == 0 && tid == 0) *a.count_out = pl.U;
@@ -298,8 +304,10 @@ ffn_tc_kernel(const __grid_constant__ TcMaps maps, const TcArgs a) {
         emit_ids(bits, prefix, W, un.tile * kTileM, min(pl.U, un.tile * kTileM + kTileM), kTileM, a.f,
                  gu_ids + u * kTileM);
     }
+    if (tid == 0) stamp(a, kTrGuIds);
     const Unit dn = unit_of(pl, c, grid, n_gu, ns);
     if (dn.kind == 1) emit_ids(bits, prefix, W, dn.P0, dn.P1, dn.stages * ns, a.f, dn_ids);
+    if (tid == 0) stamp(a, kTrDnIds);
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = ctl->tmem_base;

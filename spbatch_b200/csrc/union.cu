@@ -39,7 +39,7 @@ union_bits_kernel(const float *__restrict__ idx, int B, int f, int W, int G, uin
         const bool in = j < f;
         uint32_t seg = 0;
         int t = 0;
-        constexpr int U = 8;
+        constexpr int U = 32;  // all of a 32-token batch's labels in flight at once
         for (; t + U <= B; t += U) {
             float v[U];
 #pragma unroll
