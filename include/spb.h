@@ -103,6 +103,27 @@ int spb_ffn_forward(const void *w_gate, const void *w_up, const void *w_down, in
                     void *stream);
 
 /*
+ * Low-rank activity predictor (DejaVu MLP): the batch's active-neuron sets.
+ * The reference has it only as a PyTorch model (DejaVu_predictor/main_mlp.py:
+ * 137-141, Linear(d,D) -> ReLU -> Linear(D,f), no biases) with the decision
+ * sigmoid(logit) >= 0.5 (trainer_mlp.py:35-37).
+ *   p1 [D][d] fp16 (fc1.weight), p2 [f][D] fp16 (fc2.weight), x [B][d] fp32
+ *   hidden = fp16(ReLU(p1 . fp16(x))), logit = p2 . hidden (fp32, a fixed
+ *   reduction order, so logits and index sets reproduce bit-for-bit)
+ *   k > 0: the k largest logits per token are active (ties -> lower id);
+ *   k = 0: logit >= threshold is active (threshold 0 = sigmoid >= 0.5)
+ *   labels_out [B][f] fp32: 1 active / 0 inactive -- the label format
+ *              spb_union / spb_ffn_forward consume
+ *   idx_out    [B][k > 0 ? k : f] (nullable): ascending active ids per token
+ *   count_out  [B] (nullable), logits_out [B][f] (nullable)
+ * d and D must be multiples of 256; workspace: spb_predict_workspace_bytes.
+ */
+size_t spb_predict_workspace_bytes(int B, int D, int f);
+int spb_predict(const void *p1, const void *p2, const float *x, int B, int d, int D, int f, int k, float threshold,
+                float *labels_out, int32_t *idx_out, int32_t *count_out, float *logits_out, void *workspace,
+                size_t workspace_bytes, void *stream);
+
+/*
  * Allocation-free variant of spb_union for callers that cannot allocate
  * device memory (a framework allocator owns the device, a plug-in receives
  * only its input and output buffers, or a latency-critical path must not call

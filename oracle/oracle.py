@@ -57,6 +57,7 @@ def lib():
         _lib.spbo_quantize_q8_0.argtypes = [P, i, i, P]
         _lib.spbo_quantize_q4_0.argtypes = [P, i, i, P]
         _lib.spbo_dequantize.argtypes = [P, i, i, i, P]
+        _lib.spbo_predict.argtypes = [P, P, P, i, i, i, i, i, C.c_float, P, P, P, P]
     return _lib
 
 
@@ -199,3 +200,18 @@ def ref_naive_sparsity_div(idx: np.ndarray):
     act = np.zeros(groups, np.int32)
     fn(_p(idx), _p(merge), _p(act), B, f)
     return merge, act
+
+
+def predict(p1, p2, x, k=0, threshold=0.0):
+    """Predictor oracle: (logits [B][f], labels [B][f], idx [B][cap], counts [B])."""
+    p1, p2 = _u16(p1), _u16(p2)
+    x = _f32(x)
+    B, d = x.shape
+    D, f = p1.shape[0], p2.shape[0]
+    cap = k if k > 0 else f
+    logits = np.zeros((B, f), np.float32)
+    labels = np.zeros((B, f), np.float32)
+    idx = np.full((B, cap), -1, np.int32)
+    counts = np.zeros(B, np.int32)
+    lib().spbo_predict(_p(p1), _p(p2), _p(x), B, d, D, f, k, threshold, _p(logits), _p(labels), _p(idx), _p(counts))
+    return logits, labels, idx, counts

@@ -357,3 +357,90 @@ void spbo_ffn_f32w(const float *wg, const float *wu, const float *wd, const floa
     free(counts);
     free(merge);
 }
+
+/* ---------------- low-rank predictor -------------------------------------- */
+
+/*
+ * Dot product in the fixed order the GPU predictor uses
+ * (spbatch_b200/csrc/predict.cu): 32 lanes, lane l accumulates the 8-element
+ * chunks l, l+32, ... in order with fused multiply-adds; then lanes are added
+ * pairwise, v[l] + v[l ^ o] for o = 16, 8, 4, 2, 1.  n % 256 == 0.
+ */
+static float fixed_dot(const uint16_t *w, const float *v, int n) {
+    float acc[32], nxt[32];
+    for (int l = 0; l < 32; ++l) acc[l] = 0.0f;
+    for (int c = 0; c < n / 8; ++c) {
+        int l = c % 32;
+        for (int e = 0; e < 8; ++e) acc[l] = fmaf(spbo_f16_to_f32(w[c * 8 + e]), v[c * 8 + e], acc[l]);
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        for (int l = 0; l < 32; ++l) nxt[l] = acc[l] + acc[l ^ o];
+        for (int l = 0; l < 32; ++l) acc[l] = nxt[l];
+    }
+    return acc[0];
+}
+
+static uint32_t order_key(float v) {
+    uint32_t b;
+    memcpy(&b, &v, 4);
+    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
+/*
+ * DejaVu predictor (DejaVu_predictor/main_mlp.py:137-141: Linear(d, D) ->
+ * ReLU -> Linear(D, f), no biases; decision sigmoid >= 0.5,
+ * trainer_mlp.py:35-37):
+ *   hidden = fp16(ReLU(P1 . fp16(x))), logit = P2 . hidden (fixed order)
+ *   k > 0: top-k logits active (ties -> lower neuron id); k == 0: logit >= thr.
+ * Outputs logits [B][f], labels [B][f] (1/0), idx [B][cap] ascending with
+ * cap = k > 0 ? k : f, counts [B].
+ */
+void spbo_predict(const uint16_t *p1, const uint16_t *p2, const float *x, int B, int d, int D, int f, int k,
+                  float thr, float *logits, float *labels, int32_t *idx, int32_t *counts) {
+    float *xr = (float *)malloc(sizeof(float) * d);
+    float *hid = (float *)malloc(sizeof(float) * D);
+    int32_t *order = (int32_t *)malloc(sizeof(int32_t) * f);
+    uint32_t *keys = (uint32_t *)malloc(sizeof(uint32_t) * f);
+    int cap = k > 0 ? k : f;
+    for (int t = 0; t < B; ++t) {
+        for (int i = 0; i < d; ++i) xr[i] = r16(x[(int64_t)t * d + i]);
+        for (int r = 0; r < D; ++r) {
+            float h = fixed_dot(p1 + (int64_t)r * d, xr, d);
+            hid[r] = r16(h > 0.0f ? h : 0.0f);
+        }
+        float *lg = logits + (int64_t)t * f;
+        for (int j = 0; j < f; ++j) lg[j] = fixed_dot(p2 + (int64_t)j * D, hid, D);
+        float *lab = labels + (int64_t)t * f;
+        for (int j = 0; j < f; ++j) lab[j] = 0.0f;
+        if (k >= f) {
+            for (int j = 0; j < f; ++j) lab[j] = 1.0f;
+        } else if (k > 0) {
+            /* selection by (key desc, index asc): k passes of a partial
+             * selection would be slow; sort indices instead (insertion into a
+             * heap is unnecessary at test sizes) */
+            for (int j = 0; j < f; ++j) { order[j] = j; keys[j] = order_key(lg[j]); }
+            /* simple stable counting: the k-th largest key by scanning */
+            for (int a = 0; a < k; ++a) {
+                int best = -1;
+                for (int j = 0; j < f; ++j) {
+                    if (lab[j] != 0.0f) continue;
+                    if (best < 0 || keys[j] > keys[best]) best = j; /* ties keep the lower j */
+                }
+                lab[best] = 1.0f;
+            }
+        } else {
+            for (int j = 0; j < f; ++j) lab[j] = lg[j] >= thr ? 1.0f : 0.0f;
+        }
+        int n = 0;
+        for (int j = 0; j < f; ++j)
+            if (lab[j] != 0.0f) {
+                if (idx && n < cap) idx[(int64_t)t * cap + n] = j;
+                ++n;
+            }
+        if (counts) counts[t] = n;
+    }
+    free(keys);
+    free(order);
+    free(hid);
+    free(xr);
+}

@@ -42,6 +42,9 @@ def lib() -> C.CDLL:
         L.spb_ffn_workspace_bytes.restype = Z
         L.spb_union.argtypes = [P, I, I, I, P, P, P, P, Z, P]
         L.spb_union_static.argtypes = [P, I, I, I, P, P, P, P]
+        L.spb_predict_workspace_bytes.argtypes = [I, I, I]
+        L.spb_predict_workspace_bytes.restype = Z
+        L.spb_predict.argtypes = [P, P, P, I, I, I, I, I, C.c_float, P, P, P, P, P, Z, P]
         L.spb_ffn_forward.argtypes = [P, P, P, I, P, P, I, I, I, I, I, I, P, P, P, P, Z, P]
         L.spb_ffn_launches.argtypes = [I, I]
         L.spb_trace_enable.argtypes = [P, Z]
@@ -122,6 +125,28 @@ def ffn_forward(w_gate, w_up, w_down, x, idx, *, wtype: int = W_F16, act: int = 
                                  _ptr(merge_idx_out), _ptr(count_out), ws.data_ptr(), ws.numel(),
                                  _stream(stream)), "spb_ffn_forward")
     return out
+
+
+def predict(p1, p2, x, k: int = 0, threshold: float = 0.0, *, return_idx: bool = False, stream=None):
+    """DejaVu predictor on the GPU (spb_predict): labels [B][f] (1 active).
+
+    p1 [D][d] fp16, p2 [f][D] fp16, x [B][d] fp32.  k > 0 selects the top-k
+    logits per token; k = 0 thresholds the logits.  With return_idx, also the
+    ascending active ids [B][k or f] and the per-token counts.
+    """
+    import torch
+    _require_cuda(p1, p2, x)
+    B, d = x.shape
+    D, f = p1.shape[0], p2.shape[0]
+    dev = x.device
+    labels = torch.empty((B, f), dtype=torch.float32, device=dev)
+    idx = torch.full((B, k if k > 0 else f), -1, dtype=torch.int32, device=dev) if return_idx else None
+    counts = torch.zeros(B, dtype=torch.int32, device=dev) if return_idx else None
+    ws = torch.empty(int(lib().spb_predict_workspace_bytes(B, D, f)), dtype=torch.uint8, device=dev)
+    _check(lib().spb_predict(p1.data_ptr(), p2.data_ptr(), x.data_ptr(), B, d, D, f, k, threshold,
+                             labels.data_ptr(), _ptr(idx), _ptr(counts), None, ws.data_ptr(), ws.numel(),
+                             _stream(stream)), "spb_predict")
+    return (labels, idx, counts) if return_idx else labels
 
 
 class dropin:

@@ -192,6 +192,28 @@ int spb_ffn_forward(const void *w_gate, const void *w_up, const void *w_down, in
     return launch_fused_gemv(a, st);
 }
 
+size_t spb_predict_workspace_bytes(int B, int D, int f) {
+    if (B <= 0 || D <= 0 || f <= 0) return 0;
+    return align256(sizeof(__half) * (size_t)B * D) + align256(sizeof(float) * (size_t)B * f);
+}
+
+int spb_predict(const void *p1, const void *p2, const float *x, int B, int d, int D, int f, int k, float threshold,
+                float *labels_out, int32_t *idx_out, int32_t *count_out, float *logits_out, void *workspace,
+                size_t workspace_bytes, void *stream) {
+    if (!p1 || !p2 || !x || !labels_out) return fail(SPB_ERR_INVALID, "spb_predict: null pointer");
+    if (B <= 0 || d <= 0 || D <= 0 || f <= 0 || k < 0) return fail(SPB_ERR_INVALID, "spb_predict: bad shape");
+    if (d % 256 || D % 256) return fail(SPB_ERR_INVALID, "spb_predict: d and D must be multiples of 256");
+    if (!aligned16(p1) || !aligned16(p2)) return fail(SPB_ERR_INVALID, "spb_predict: weights must be 16-byte aligned");
+    const size_t need = spb_predict_workspace_bytes(B, D, f);
+    if (!workspace || workspace_bytes < need) return fail(SPB_ERR_WORKSPACE, "spb_predict: workspace too small");
+    __half *hidden = static_cast<__half *>(workspace);
+    float *logits = logits_out ? logits_out
+                               : reinterpret_cast<float *>(static_cast<char *>(workspace) +
+                                                           align256(sizeof(__half) * (size_t)B * D));
+    return launch_predict(static_cast<const __half *>(p1), static_cast<const __half *>(p2), x, B, d, D, f, k,
+                          threshold, labels_out, idx_out, count_out, logits, hidden, static_cast<cudaStream_t>(stream));
+}
+
 int spb_trace_enable(void *device_buffer, size_t slots) {
     std::lock_guard<std::mutex> lk(g_trace_mu);
     g_trace_buf = device_buffer;

@@ -62,4 +62,9 @@ struct TcLaunch {
 };
 int launch_ffn_tc(const TcLaunch &L, cudaStream_t st);
 
+// predict.cu -- low-rank activity predictor
+int launch_predict(const __half *p1, const __half *p2, const float *x, int B, int d, int D, int f, int k,
+                   float threshold, float *labels, int32_t *idx, int32_t *counts, float *logits, __half *hidden,
+                   cudaStream_t st);
+
 }  // namespace spb

@@ -1,0 +1,91 @@
+"""GPU parity of the low-rank predictor: logits, label sets and ascending
+index lists bit-exact against the CPU oracle (both use one fixed fp32
+reduction order)."""
+import numpy as np
+import pytest
+
+from conftest import assert_close
+
+pytestmark = pytest.mark.gpu
+
+
+def _dev(a, dev):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+
+
+def _weights(rng, d, D, f):
+    p1 = (rng.standard_normal((D, d)) / np.sqrt(d)).astype(np.float16)
+    p2 = (rng.standard_normal((f, D)) / np.sqrt(D)).astype(np.float16)
+    return p1, p2
+
+
+def _run(spb, cuda, p1, p2, x, k, thr=0.0):
+    import torch
+    B, f = x.shape[0], p2.shape[0]
+    D = p1.shape[0]
+    P1, P2, X = _dev(p1, cuda), _dev(p2, cuda), _dev(x, cuda)
+    labels = torch.empty((B, f), device=cuda)
+    cap = k if k > 0 else f
+    idx = torch.full((B, cap), -1, dtype=torch.int32, device=cuda)
+    counts = torch.zeros(B, dtype=torch.int32, device=cuda)
+    logits = torch.empty((B, f), device=cuda)
+    ws = torch.zeros(int(spb.lib().spb_predict_workspace_bytes(B, D, f)), dtype=torch.uint8, device=cuda)
+    rc = spb.lib().spb_predict(P1.data_ptr(), P2.data_ptr(), X.data_ptr(), B, x.shape[1], D, f, k, thr,
+                               labels.data_ptr(), idx.data_ptr(), counts.data_ptr(), logits.data_ptr(), ws.data_ptr(),
+                               ws.numel(), torch.cuda.current_stream().cuda_stream)
+    assert rc == 0, spb.lib().spb_last_error()
+    torch.cuda.synchronize()
+    return logits.cpu().numpy(), labels.cpu().numpy(), idx.cpu().numpy(), counts.cpu().numpy()
+
+
+@pytest.mark.parametrize("B,d,D,f,k", [(1, 4096, 1024, 11008, 1101), (4, 512, 256, 1000, 100), (19, 1024, 512, 2048, 300),
+                                       (64, 5120, 1024, 13824, 1106)])
+def test_predict_bit_exact(spb, cuda, oracle_mod, B, d, D, f, k):
+    rng = np.random.default_rng(B * 7 + f)
+    p1, p2 = _weights(rng, d, D, f)
+    x = rng.standard_normal((B, d)).astype(np.float32)
+    g = _run(spb, cuda, p1, p2, x, k)
+    want = oracle_mod.predict(p1, p2, x, k=k)
+    for got, ref, name in zip(g, want, ("logits", "labels", "idx", "counts")):
+        np.testing.assert_array_equal(got, ref, err_msg=name)
+
+
+def test_predict_ties_go_to_lower_ids(spb, cuda, oracle_mod):
+    rng = np.random.default_rng(3)
+    B, d, D, f, k = 2, 512, 256, 512, 37
+    p1, p2 = _weights(rng, d, D, f)
+    p2[100:200] = p2[5]  # 100 neurons share one logit per token
+    x = rng.standard_normal((B, d)).astype(np.float32)
+    g = _run(spb, cuda, p1, p2, x, k)
+    want = oracle_mod.predict(p1, p2, x, k=k)
+    for got, ref in zip(g, want):
+        np.testing.assert_array_equal(got, ref)
+
+
+@pytest.mark.parametrize("k", [0, 512])
+def test_predict_threshold_and_all(spb, cuda, oracle_mod, k):
+    rng = np.random.default_rng(4)
+    B, d, D, f = 3, 256, 256, 512
+    p1, p2 = _weights(rng, d, D, f)
+    x = rng.standard_normal((B, d)).astype(np.float32)
+    g = _run(spb, cuda, p1, p2, x, k, 0.0)
+    want = oracle_mod.predict(p1, p2, x, k=k, threshold=0.0)
+    for got, ref in zip(g, want):
+        np.testing.assert_array_equal(got, ref)
+
+
+def test_predict_then_ffn_config1(spb, cuda, oracle_mod):
+    """Config 1: predictor picks exactly 1101 of 11008 neurons, then the sparse FFN."""
+    import torch
+    rng = np.random.default_rng(0)
+    B, d, D, f, k = 1, 4096, 1024, 11008, 1101
+    p1, p2 = _weights(rng, d, D, f)
+    W = [(rng.standard_normal((f, d)) * 0.02).astype(np.float16) for _ in range(3)]
+    x = rng.standard_normal((B, d)).astype(np.float32)
+    labels = spb.predict(_dev(p1, cuda), _dev(p2, cuda), _dev(x, cuda), k=k)
+    out = spb.ffn_forward(*[_dev(w, cuda) for w in W], _dev(x, cuda), labels)
+    torch.cuda.synchronize()
+    _, lab_ref, _, _ = oracle_mod.predict(p1, p2, x, k=k)
+    np.testing.assert_array_equal(labels.cpu().numpy(), lab_ref)
+    assert_close(out.cpu().numpy(), oracle_mod.ffn(*W, x, lab_ref))

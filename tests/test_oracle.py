@@ -128,3 +128,22 @@ def test_q4_0_nibble_placement(oracle_mod):
     assert q[0, 3] & 0xF == 0 and q[0, 3] >> 4 == 12
     deq = oracle_mod.dequantize(q, 4, 32)
     assert deq[0, 3] == -8.0 and deq[0, 19] == 4.0
+
+
+def test_predictor_oracle_vs_numpy(oracle_mod):
+    rng = np.random.default_rng(21)
+    B, d, D, f = 3, 512, 256, 1024
+    p1 = (rng.standard_normal((D, d)) / np.sqrt(d)).astype(np.float16)
+    p2 = (rng.standard_normal((f, D)) / np.sqrt(D)).astype(np.float16)
+    x = rng.standard_normal((B, d)).astype(np.float32)
+    lg, lab, idx, counts = oracle_mod.predict(p1, p2, x, k=100)
+    h = np.maximum(x.astype(np.float16).astype(np.float64) @ p1.astype(np.float64).T, 0)
+    ref = h.astype(np.float16).astype(np.float64) @ p2.astype(np.float64).T
+    assert np.abs(ref - lg).max() < 1e-4
+    assert (counts == 100).all() and (lab.sum(1) == 100).all()
+    for t in range(B):
+        order = np.lexsort((np.arange(f), -lg[t]))  # logit desc, id asc
+        np.testing.assert_array_equal(idx[t], np.sort(order[:100]))
+    _, lab0, _, c0 = oracle_mod.predict(p1, p2, x, k=0, threshold=0.0)
+    np.testing.assert_array_equal(lab0, (lg >= 0).astype(np.float32))
+    assert (c0 == lab0.sum(1)).all()
