@@ -103,6 +103,21 @@ int spb_ffn_forward(const void *w_gate, const void *w_up, const void *w_down, in
                     void *stream);
 
 /*
+ * Block-quantised weights (BASELINE: ggml Q8_0 / Q4_0; the reference has only
+ * the f16 instance of its block-dequantisation hook, cuda/kernel.cuh:69,
+ * cuda/kernel.cu:337-356).  Rows use the "split" layout: all quant bytes of
+ * the row, then its d/32 fp16 block scales.
+ *   spb_weight_row_bytes  bytes of one stored row (d % 32 == 0), -1 if invalid
+ *   spb_quantize          host-side quantisation of rows x d fp32 weights
+ *   spb_dequantize_rows   device decoding with the gather kernels' own
+ *                         in-register dequantisation (d % 256 == 0)
+ * spb_ffn_forward accepts wtype SPB_W_Q8_0 / SPB_W_Q4_0 on the CUDA-core path.
+ */
+int64_t spb_weight_row_bytes(int wtype, int d);
+int spb_quantize(const float *w, int rows, int d, int wtype, uint8_t *out);
+int spb_dequantize_rows(const void *q, int wtype, int rows, int d, float *out, void *stream);
+
+/*
  * Low-rank activity predictor (DejaVu MLP): the batch's active-neuron sets.
  * The reference has it only as a PyTorch model (DejaVu_predictor/main_mlp.py:
  * 137-141, Linear(d,D) -> ReLU -> Linear(D,f), no biases) with the decision

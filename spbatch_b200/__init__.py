@@ -42,6 +42,10 @@ def lib() -> C.CDLL:
         L.spb_ffn_workspace_bytes.restype = Z
         L.spb_union.argtypes = [P, I, I, I, P, P, P, P, Z, P]
         L.spb_union_static.argtypes = [P, I, I, I, P, P, P, P]
+        L.spb_weight_row_bytes.argtypes = [I, I]
+        L.spb_weight_row_bytes.restype = C.c_int64
+        L.spb_quantize.argtypes = [P, I, I, I, P]
+        L.spb_dequantize_rows.argtypes = [P, I, I, I, P, P]
         L.spb_predict_workspace_bytes.argtypes = [I, I, I]
         L.spb_predict_workspace_bytes.restype = Z
         L.spb_predict.argtypes = [P, P, P, I, I, I, I, I, C.c_float, P, P, P, P, P, Z, P]
@@ -124,6 +128,20 @@ def ffn_forward(w_gate, w_up, w_down, x, idx, *, wtype: int = W_F16, act: int = 
                                  idx.data_ptr(), B, d, f, act, int(per_token_mask), path, out.data_ptr(),
                                  _ptr(merge_idx_out), _ptr(count_out), ws.data_ptr(), ws.numel(),
                                  _stream(stream)), "spb_ffn_forward")
+    return out
+
+
+def quantize(w, wtype: int):
+    """Host-side ggml quantisation of fp32 rows ([rows][d] numpy) to the split
+    row layout; returns a [rows][row_bytes] uint8 numpy array."""
+    import numpy as np
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    rows, d = w.shape
+    rb = int(lib().spb_weight_row_bytes(wtype, d))
+    if rb <= 0:
+        raise SpbError("quantize: d must be a multiple of 32")
+    out = np.zeros((rows, rb), np.uint8)
+    _check(lib().spb_quantize(w.ctypes.data, rows, d, wtype, out.ctypes.data), "spb_quantize")
     return out
 
 

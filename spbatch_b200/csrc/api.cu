@@ -119,7 +119,8 @@ int spb_ffn_forward(const void *w_gate, const void *w_up, const void *w_down, in
         return fail(SPB_ERR_WORKSPACE, "spb_ffn_forward: workspace too small");
     cudaStream_t st = static_cast<cudaStream_t>(stream);
 
-    if (path == SPB_PATH_AUTO) path = B <= kGemvMaxBatch ? SPB_PATH_GEMV : SPB_PATH_TENSOR;
+    // quantised weights are served by the CUDA-core path (in-register dequantisation)
+    if (path == SPB_PATH_AUTO) path = (B <= kGemvMaxBatch || wtype != SPB_W_F16) ? SPB_PATH_GEMV : SPB_PATH_TENSOR;
     int32_t *merge = merge_idx_out ? merge_idx_out : ws.merge_idx;
     int32_t *count = count_out ? count_out : ws.counts;
 
@@ -165,7 +166,6 @@ int spb_ffn_forward(const void *w_gate, const void *w_up, const void *w_down, in
         return launch_ffn_tc(L, st);
     }
     if (path != SPB_PATH_GEMV) return fail(SPB_ERR_INVALID, "spb_ffn_forward: unknown path");
-    if (B > kGemvMaxBatch) return fail(SPB_ERR_UNSUPPORTED, "spb_ffn_forward: CUDA-core path serves B <= 4");
 
     PrepJobs jobs;
     jobs.zero_out = out;
@@ -222,7 +222,7 @@ int spb_trace_enable(void *device_buffer, size_t slots) {
 }
 
 int spb_ffn_launches(int B, int path) {
-    if (path == SPB_PATH_AUTO) path = B <= kGemvMaxBatch ? SPB_PATH_GEMV : SPB_PATH_TENSOR;
+    if (path == SPB_PATH_AUTO) path = B <= kGemvMaxBatch ? SPB_PATH_GEMV : SPB_PATH_TENSOR;  // fp16 weights
     return path == SPB_PATH_TENSOR ? 2 : 3;
 }
 

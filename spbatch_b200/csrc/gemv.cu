@@ -21,6 +21,7 @@
 // host.
 #include "spb_internal.h"
 #include "spb_scan.cuh"
+#include "spb_quant.cuh"
 
 namespace spb {
 
@@ -102,8 +103,54 @@ __device__ __forceinline__ float apply_act(float g, float u, int act) {
 }
 
 // ---- fused path -----------------------------------------------------------
+//
+// Weight formats (one row per neuron, rows 16-byte aligned):
+//   SPB_W_F16   d fp16 values
+//   SPB_W_Q8_0  d int8 quants, then d/32 fp16 block scales; w = q * scale
+//   SPB_W_Q4_0  d/2 bytes (block b: byte j holds element j in its low nibble
+//               and element j + 16 in its high nibble), then d/32 fp16 scales;
+//               w = (nibble - 8) * scale
+// Dequantisation happens in registers: (float)q * (float)scale, the same
+// single fp32 rounding the oracle performs, so dequantised values are
+// identical.
 
-template <int NT>
+// NT dot products of the gate and up rows with the activations in shared
+// memory (xs[t][0..d)); per-lane partial sums reduced across the warp.
+template <int NT, int WT>
+__device__ __forceinline__ void row_dot2_q(const uint8_t *__restrict__ rg, const uint8_t *__restrict__ ru,
+                                           const float *__restrict__ xs, int d, int nt, float (&ag)[NT],
+                                           float (&au)[NT]) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int t = 0; t < NT; ++t) ag[t] = au[t] = 0.0f;
+    for (int c = lane; c < d / 8; c += 32) {
+        float wg[8], wu[8];
+        fetch8<WT>(rg, d, c * 8, wg);
+        fetch8<WT>(ru, d, c * 8, wu);
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+            if (t < nt) {
+                const float4 *xp = reinterpret_cast<const float4 *>(xs + (int64_t)t * d + c * 8);
+                const float4 x0 = xp[0], x1 = xp[1];
+                const float xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    ag[t] = fmaf(wg[k], xv[k], ag[t]);
+                    au[t] = fmaf(wu[k], xv[k], au[t]);
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+        ag[t] = warp_sum(ag[t]);
+        au[t] = warp_sum(au[t]);
+    }
+}
+
+// Tokens are processed in groups of NT (the activations of a group sit in
+// shared memory); weights are re-read per group, mostly from L2.
+template <int NT, int WT>
 __global__ void __launch_bounds__(kGemvThreads) fused_gateup_gemv_kernel(FusedGemvArgs a) {
     extern __shared__ __align__(16) float smem[];
     const int W = words_of(a.f);
@@ -112,7 +159,6 @@ __global__ void __launch_bounds__(kGemvThreads) fused_gateup_gemv_kernel(FusedGe
     int *wtot = prefix + W + 1;
     int *nid = wtot + 64;
 
-    load_x_rounded<NT>(a.x, a.B, 0, a.d, xs);
     scan_popc(a.seg_bits, W, prefix, wtot);
     const int U = prefix[W];
     const int p0 = (int)((int64_t)U * blockIdx.x / gridDim.x);
@@ -123,24 +169,29 @@ __global__ void __launch_bounds__(kGemvThreads) fused_gateup_gemv_kernel(FusedGe
     for (int i = threadIdx.x; i < p1 - p0; i += blockDim.x) a.merge[p0 + i] = nid[i];
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const __half *wg = static_cast<const __half *>(a.wg);
-    const __half *wu = static_cast<const __half *>(a.wu);
-    for (int i = warp; i < p1 - p0; i += kGemvWarps) {
-        const int j = nid[i];
-        float ag[NT], au[NT];
+    const int64_t rb = row_bytes_of<WT>(a.d);
+    const uint8_t *wg = static_cast<const uint8_t *>(a.wg);
+    const uint8_t *wu = static_cast<const uint8_t *>(a.wu);
+    for (int t0 = 0; t0 < a.B; t0 += NT) {
+        const int nt = min(NT, a.B - t0);
+        __syncthreads();
+        load_x_rounded<NT>(a.x, a.B, t0, a.d, xs);
+        __syncthreads();
+        for (int i = warp; i < p1 - p0; i += kGemvWarps) {
+            const int j = nid[i];
+            float ag[NT], au[NT];
+            row_dot2_q<NT, WT>(wg + j * rb, wu + j * rb, xs, a.d, nt, ag, au);
+            if (lane == 0) {
 #pragma unroll
-        for (int t = 0; t < NT; ++t) ag[t] = au[t] = 0.0f;
-        row_dot2<NT>(wg + (int64_t)j * a.d, wu + (int64_t)j * a.d, xs, a.d, ag, au);
-        if (lane == 0) {
-#pragma unroll
-            for (int t = 0; t < NT; ++t) {
-                if (t < a.B) {
-                    float hv = apply_act(ag[t], au[t], a.act);
-                    if (a.per_token) {
-                        const uint32_t word = a.tok_bits[(int64_t)t * W + (j >> 5)];
-                        if (!((word >> (j & 31)) & 1u)) hv = 0.0f;
+                for (int t = 0; t < NT; ++t) {
+                    if (t < nt) {
+                        float hv = apply_act(ag[t], au[t], a.act);
+                        if (a.per_token) {
+                            const uint32_t word = a.tok_bits[(int64_t)(t0 + t) * W + (j >> 5)];
+                            if (!((word >> (j & 31)) & 1u)) hv = 0.0f;
+                        }
+                        a.h[(int64_t)(p0 + i) * a.B + t0 + t] = __float2half_rn(hv);
                     }
-                    a.h[(int64_t)(p0 + i) * a.B + t] = __float2half_rn(hv);
                 }
             }
         }
@@ -150,65 +201,62 @@ __global__ void __launch_bounds__(kGemvThreads) fused_gateup_gemv_kernel(FusedGe
 constexpr int kDownCols = kGemvThreads * 8;  // output columns per CTA
 constexpr int kDownUnroll = 8;               // rows in flight per thread
 
-template <int NT>
+template <int NT, int WT>
 __global__ void __launch_bounds__(kGemvThreads) fused_down_gemv_kernel(FusedGemvArgs a, int cap) {
     extern __shared__ __align__(16) float smem[];
-    float *hs = smem;                                   // [cap][NT]
-    int *nid = reinterpret_cast<int *>(hs + cap * NT);  // [cap]
+    int *nid = reinterpret_cast<int *>(smem);             // [cap]
+    float *hs = smem + cap;                               // [cap][NT]
     const int U = *a.count;
     const int p0 = (int)((int64_t)U * blockIdx.y / gridDim.y);
     const int p1 = (int)((int64_t)U * (blockIdx.y + 1) / gridDim.y);
     const int n = p1 - p0;
     for (int i = threadIdx.x; i < n; i += blockDim.x) nid[i] = a.merge[p0 + i];
-    for (int i = threadIdx.x; i < n * NT; i += blockDim.x) {
-        const int p = i / NT, t = i - p * NT;
-        hs[i] = t < a.B ? __half2float(a.h[(int64_t)(p0 + p) * a.B + t]) : 0.0f;
-    }
-    __syncthreads();
     const int m = blockIdx.x * kDownCols + threadIdx.x * 8;
-    if (m >= a.d || n == 0) return;
-    const __half *wd = static_cast<const __half *>(a.wd) + m;
-    float acc[NT][8];
+    const int64_t rb = row_bytes_of<WT>(a.d);
+    const uint8_t *wd = static_cast<const uint8_t *>(a.wd);
+    for (int t0 = 0; t0 < a.B; t0 += NT) {
+        const int nt = min(NT, a.B - t0);
+        __syncthreads();
+        for (int i = threadIdx.x; i < n * NT; i += blockDim.x) {
+            const int p = i / NT, t = i - p * NT;
+            hs[i] = t < nt ? __half2float(a.h[(int64_t)(p0 + p) * a.B + t0 + t]) : 0.0f;
+        }
+        __syncthreads();
+        if (m >= a.d || n == 0) continue;
+        float acc[NT][8];
 #pragma unroll
-    for (int t = 0; t < NT; ++t)
+        for (int t = 0; t < NT; ++t)
 #pragma unroll
-        for (int k = 0; k < 8; ++k) acc[t][k] = 0.0f;
-    for (int p = 0; p < n; p += kDownUnroll) {
-        uint4 v[kDownUnroll];
+            for (int k = 0; k < 8; ++k) acc[t][k] = 0.0f;
+        for (int p = 0; p < n; p += kDownUnroll) {
+            float w[kDownUnroll][8];
 #pragma unroll
-        for (int u = 0; u < kDownUnroll; ++u)
-            if (p + u < n) v[u] = ld_stream_v4(wd + (int64_t)nid[p + u] * a.d);
+            for (int u = 0; u < kDownUnroll; ++u)
+                if (p + u < n) fetch8<WT>(wd + nid[p + u] * rb, a.d, m, w[u]);
 #pragma unroll
-        for (int u = 0; u < kDownUnroll; ++u) {
-            if (p + u < n) {
-                const uint32_t *pv = reinterpret_cast<const uint32_t *>(&v[u]);
-                float w[8];
+            for (int u = 0; u < kDownUnroll; ++u) {
+                if (p + u < n) {
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    float2 f2 = h2f2(pv[q]);
-                    w[2 * q] = f2.x;
-                    w[2 * q + 1] = f2.y;
-                }
+                    for (int t = 0; t < NT; ++t) {
+                        const float hv = hs[(p + u) * NT + t];
 #pragma unroll
-                for (int t = 0; t < NT; ++t) {
-                    const float hv = hs[(p + u) * NT + t];
-#pragma unroll
-                    for (int k = 0; k < 8; ++k) acc[t][k] = fmaf(w[k], hv, acc[t][k]);
+                        for (int k = 0; k < 8; ++k) acc[t][k] = fmaf(w[u][k], hv, acc[t][k]);
+                    }
                 }
             }
         }
-    }
 #pragma unroll
-    for (int t = 0; t < NT; ++t) {
-        if (t < a.B) {
-            float4 *o = reinterpret_cast<float4 *>(a.out + (int64_t)t * a.d + m);
-            atomicAdd(o, make_float4(acc[t][0], acc[t][1], acc[t][2], acc[t][3]));
-            atomicAdd(o + 1, make_float4(acc[t][4], acc[t][5], acc[t][6], acc[t][7]));
+        for (int t = 0; t < NT; ++t) {
+            if (t < nt) {
+                float4 *o = reinterpret_cast<float4 *>(a.out + (int64_t)(t0 + t) * a.d + m);
+                atomicAdd(o, make_float4(acc[t][0], acc[t][1], acc[t][2], acc[t][3]));
+                atomicAdd(o + 1, make_float4(acc[t][4], acc[t][5], acc[t][6], acc[t][7]));
+            }
         }
     }
 }
 
-template <int NT>
+template <int NT, int WT>
 static int launch_fused_gemv_nt(const FusedGemvArgs &a, cudaStream_t st) {
     const int sms = num_sms();
     const int W = words_of(a.f);
@@ -217,7 +265,7 @@ static int launch_fused_gemv_nt(const FusedGemvArgs &a, cudaStream_t st) {
     const int cap_g = a.f / grid + 2;
     size_t smem_g = sizeof(float) * NT * a.d + sizeof(int) * (W + 1 + 64 + cap_g);
     if (smem_g > 200 * 1024) return fail(SPB_ERR_UNSUPPORTED, "gemv: d too large for shared-memory staging");
-    auto kg = fused_gateup_gemv_kernel<NT>;
+    auto kg = fused_gateup_gemv_kernel<NT, WT>;
     if (int rc_ = ensure_smem((const void *)kg, smem_g)) return rc_;
     kg<<<grid, kGemvThreads, smem_g, st>>>(a);
     SPB_LAUNCH_CHECK("fused_gateup_gemv_kernel");
@@ -226,19 +274,27 @@ static int launch_fused_gemv_nt(const FusedGemvArgs &a, cudaStream_t st) {
     const int chunks = (2 * sms + slices - 1) / slices;
     const int cap_d = a.f / chunks + 2;
     size_t smem_d = (sizeof(float) * NT + sizeof(int)) * cap_d;
-    auto kd = fused_down_gemv_kernel<NT>;
+    auto kd = fused_down_gemv_kernel<NT, WT>;
     if (int rc_ = ensure_smem((const void *)kd, smem_d)) return rc_;
     kd<<<dim3(slices, chunks), kGemvThreads, smem_d, st>>>(a, cap_d);
     SPB_LAUNCH_CHECK("fused_down_gemv_kernel");
     return SPB_OK;
 }
 
+template <int WT>
+static int launch_fused_gemv_wt(const FusedGemvArgs &a, cudaStream_t st) {
+    if (a.B <= 1) return launch_fused_gemv_nt<1, WT>(a, st);
+    if (a.B <= 2) return launch_fused_gemv_nt<2, WT>(a, st);
+    return launch_fused_gemv_nt<4, WT>(a, st);
+}
+
 int launch_fused_gemv(const FusedGemvArgs &a, cudaStream_t st) {
-    if (a.wtype != SPB_W_F16) return fail(SPB_ERR_UNSUPPORTED, "gemv: weight type not built yet");
-    if (a.B <= 1) return launch_fused_gemv_nt<1>(a, st);
-    if (a.B <= 2) return launch_fused_gemv_nt<2>(a, st);
-    if (a.B <= 4) return launch_fused_gemv_nt<4>(a, st);
-    return fail(SPB_ERR_UNSUPPORTED, "gemv path serves B <= 4");
+    switch (a.wtype) {
+        case SPB_W_F16: return launch_fused_gemv_wt<SPB_W_F16>(a, st);
+        case SPB_W_Q8_0: return launch_fused_gemv_wt<SPB_W_Q8_0>(a, st);
+        case SPB_W_Q4_0: return launch_fused_gemv_wt<SPB_W_Q4_0>(a, st);
+        default: return fail(SPB_ERR_INVALID, "gemv: unknown weight type");
+    }
 }
 
 // ---- drop-in (segment) path -------------------------------------------------

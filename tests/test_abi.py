@@ -71,3 +71,16 @@ def test_python_wrappers_refuse_cpu_tensors(spb):
     x = torch.zeros(2, 64)
     with pytest.raises(spb.SpbError):
         spb.ffn_forward(x, x, x, x, x)
+
+
+def test_library_quantizer_matches_oracle(spb, oracle_mod):
+    """Host-side spb_quantize produces the oracle's ggml bytes exactly."""
+    import numpy as np
+    rng = np.random.default_rng(31)
+    w = (rng.standard_normal((40, 256)) * 0.02).astype(np.float32)
+    w[0, :32] = 0.0                  # all-zero block (scale 0)
+    w[1, :32] = 0.5                  # constant block
+    w[2, 5] = -3.0                   # negative extreme sets the Q4_0 scale sign
+    for qt, code in ((8, spb.W_Q8_0), (4, spb.W_Q4_0)):
+        np.testing.assert_array_equal(spb.quantize(w, code), oracle_mod.quantize(w, qt))
+        assert spb.lib().spb_weight_row_bytes(code, 4096) == (4096 if qt == 8 else 2048) + 256
