@@ -53,6 +53,8 @@ def parse():
     ap.add_argument("--layers", type=int, default=0, help="distinct layer copies rotated (0 = auto)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-budget", type=float, default=15.0)
+    ap.add_argument("--shard", action="store_true",
+                    help="shard the layer's neurons across the torchrun ranks (config 5) instead of replicas")
     return ap.parse_args()
 
 
@@ -128,22 +130,30 @@ class Clocks:
                 "reasons": reasons, "samples": len(rows)}
 
 
-def make_layers(a, L, device, rank):
+def make_layers(a, L, device, rank, world=1):
+    """L distinct layer copies.  Replicas: each rank its own layer.  Sharded:
+    labels and x are the same on every rank (seeds without the rank) and the
+    rank holds only its rows of the weights."""
     import torch
+    from spbatch_b200.shard import shard_range
     from spbatch_b200.workload import SHAPES, zipf_active_labels
     d, f = SHAPES[a.model]["d"], SHAPES[a.model]["f"]
     k = int(round(a.activity * f))
+    seed = 0 if a.shard else rank
+    f0, f1 = shard_range(f, world, rank) if a.shard else (0, f)
     gen = torch.Generator(device=device)
     gen.manual_seed(1234 + rank)
     layers = []
     for l in range(L):
-        W = [(torch.randn((f, d), generator=gen, device=device) * 0.02).half() for _ in range(3)]
-        lab_np = zipf_active_labels(a.batch, f, k, seed=rank, layer=l)
-        x_np = np.random.default_rng([rank, l]).standard_normal((a.batch, d)).astype(np.float32)
+        W = [(torch.randn((f1 - f0, d), generator=gen, device=device) * 0.02).half() for _ in range(3)]
+        lab_full = zipf_active_labels(a.batch, f, k, seed=seed, layer=l)
+        lab_np = np.ascontiguousarray(lab_full[:, f0:f1])
+        x_np = np.random.default_rng([seed, l]).standard_normal((a.batch, d)).astype(np.float32)
         layers.append(dict(i=l, W=W, lab_np=lab_np, x_np=x_np, U=int((lab_np > 0).any(0).sum()),
+                           U_full=int((lab_full > 0).any(0).sum()),
                            lab=torch.from_numpy(lab_np).to(device), x=torch.from_numpy(x_np).to(device),
                            out=torch.empty((a.batch, d), device=device)))
-    return d, f, k, layers
+    return d, f1 - f0, k, layers
 
 
 def run_ours(a):
@@ -162,15 +172,22 @@ def run_ours(a):
     from spbatch_b200.workload import SHAPES
     d0, f0 = SHAPES[a.model]["d"], SHAPES[a.model]["f"]
     est = active_bytes(d0, min(f0, int(a.activity * f0 * min(a.batch, 8))), a.batch)
+    if a.shard:
+        est /= ws_n
     L = a.layers or int(min(32, max(4, math.ceil(3 * L2_BYTES / est))))
-    d, f, k, layers = make_layers(a, L, device, rank)
+    d, f, k, layers = make_layers(a, L, device, rank, ws_n)
     ws = spb.new_workspace(a.batch, d, f, 0, device)
     Us = [ly["U"] for ly in layers]
     bytes_per_step = float(np.mean([active_bytes(d, U, a.batch) for U in Us]))
 
+    sharded = a.shard and ws_n > 1
+
     def fwd(ly, x=None, out=None):
-        spb.ffn_forward(*ly["W"], ly["x"] if x is None else x, ly["lab"], out=ly["out"] if out is None else out,
+        o = ly["out"] if out is None else out
+        spb.ffn_forward(*ly["W"], ly["x"] if x is None else x, ly["lab"], out=o,
                         per_token_mask=bool(a.per_token), path=path, workspace=ws)
+        if sharded:  # one all-reduce of the [B][d] partial outputs (NCCL)
+            torch.distributed.all_reduce(o)
 
     stream = torch.cuda.Stream(device)
     with torch.cuda.stream(stream):
@@ -234,6 +251,8 @@ def run_ours(a):
         labin[i].copy_(pinned[i]["lab"], non_blocking=True)
         spb.ffn_forward(*ly["W"], xin[i], labin[i], out=ly["out"], per_token_mask=bool(a.per_token), path=path,
                         workspace=ws)
+        if sharded:
+            torch.distributed.all_reduce(ly["out"])
         pinned[i]["out"].copy_(ly["out"], non_blocking=True)
 
     with torch.cuda.stream(stream):
@@ -244,7 +263,7 @@ def run_ours(a):
     ge_rem = capture(rem, e2e_body) if rem else None
     ms_e2e = timed(ge_full, ge_rem)
 
-    tokens = a.batch * K * ws_n
+    tokens = a.batch * K * (1 if sharded else ws_n)
     value = tokens / (ms / 1e3)
     peak, peak_kind = hbm_peak()
     t_step = ms / K / 1e3
@@ -252,14 +271,17 @@ def run_ours(a):
     launches_per_step = spb.lib().spb_ffn_launches(a.batch, path)
     rec = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": ws_n, "steps": K, "warmup": a.warmup,
-        "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+        "ms_per_step": ms / K, "higher_is_better": True, "scaling": "strong" if sharded else "weak",
+        "vs_baseline": None, "dtype": "f16",
         "data": "synthetic (seeded N(0,0.02^2) fp16 weights, N(0,1) x, Zipf(0.8) activity; no dataset)",
-        "config": {"workload": workload_name(a, int(np.mean(Us))), "d": d, "f": f, "batch": a.batch,
+        "config": {"workload": workload_name(a, int(np.mean([ly["U_full"] for ly in layers]))), "d": d,
+                   "f_per_gpu": f, "batch": a.batch,
                    "k_per_token": k, "union_mean": float(np.mean(Us)), "layers_rotated": L,
                    "per_token_mask": bool(a.per_token), "path": a.path,
                    "l2": f"inputs larger than L2: {L} layer copies rotated, "
                          f"{L * bytes_per_step / 1e6:.0f} MB touched per cycle vs 126 MB L2",
-                   "parallelism": f"replicas x{ws_n}" if ws_n > 1 else "single GPU"},
+                   "parallelism": (f"neuron-sharded tp{ws_n} + NCCL all-reduce" if sharded else
+                                   f"replicas x{ws_n}" if ws_n > 1 else "single GPU")},
         "roofline": {"bound": "hbm", "kernel": "whole layer (union + gate/up + down launches)",
                      "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "peak_source": f"{peak_kind} hbm_gbs", "traffic": traffic_from_profiles(a),
