@@ -205,6 +205,19 @@ def run_ours(a):
                 body(layers[i % L])
         return g
 
+    class Eager:
+        """Stands in for a graph when steps contain a collective: they are
+        launched eagerly instead of being captured."""
+
+        def __init__(self, n, body):
+            self.n, self.body = n, body
+
+        def replay(self):
+            for i in range(self.n):
+                self.body(layers[i % L])
+
+    if sharded:
+        capture = Eager  # noqa: F811  (collectives stay out of graph capture)
     g_full = capture(L, fwd) if full else None
     g_rem = capture(rem, fwd) if rem else None
 
