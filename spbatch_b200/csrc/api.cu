@@ -167,6 +167,30 @@ int spb_ffn_forward(const void *w_gate, const void *w_up, const void *w_down, in
     }
     if (path != SPB_PATH_GEMV) return fail(SPB_ERR_INVALID, "spb_ffn_forward: unknown path");
 
+    if (stream_ffn_supported(wtype, B, d)) {
+        StreamFfnArgs sa{};
+        sa.wg = w_gate;
+        sa.wu = w_up;
+        sa.wd = w_down;
+        sa.wtype = wtype;
+        sa.x = x;
+        sa.idx = idx;
+        sa.B = B;
+        sa.d = d;
+        sa.f = f;
+        sa.act = act;
+        sa.per_token = per_token_mask;
+        sa.merge_out = merge_idx_out;
+        sa.count_out = count_out;
+        sa.out = out;
+        sa.err = ws.err;
+        sa.seg_bits = ws.seg_bits;
+        sa.tok_bits = ws.tok_bits;
+        sa.grid_bar = ws.grid_bar;
+        sa.launch_ctr = ws.launch_ctr;
+        sa.zero_flag = ws.zero_flag;
+        return launch_stream_ffn(sa, st);
+    }
     PrepJobs jobs;
     jobs.zero_out = out;
     jobs.zero_n = (int64_t)B * d;
@@ -189,6 +213,7 @@ int spb_ffn_forward(const void *w_gate, const void *w_up, const void *w_down, in
     a.merge = merge;
     a.count = count;
     a.out = out;
+    a.err = ws.err;
     return launch_fused_gemv(a, st);
 }
 
@@ -223,7 +248,8 @@ int spb_trace_enable(void *device_buffer, size_t slots) {
 
 int spb_ffn_launches(int B, int path) {
     if (path == SPB_PATH_AUTO) path = B <= kGemvMaxBatch ? SPB_PATH_GEMV : SPB_PATH_TENSOR;  // fp16 weights
-    return path == SPB_PATH_TENSOR ? 2 : 3;
+    if (path == SPB_PATH_TENSOR) return 2;
+    return stream_ffn_supported(SPB_W_F16, B, 4096) ? 1 : 3;  // streaming kernel, or union + gate/up + down
 }
 
 }  // extern "C"

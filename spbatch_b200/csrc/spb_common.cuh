@@ -48,6 +48,9 @@ constexpr int kMaxTcGrid = 160;  // upper bound on the tensor-path grid (148 SMs
 
 struct Workspace {
     uint32_t *err;         // [1] sticky device error code
+    unsigned long long *launch_ctr;  // [1] streaming kernel: monotonic CTA ticket counter
+    unsigned long long *grid_bar;    // [1] streaming kernel: grid-barrier arrival counter
+    unsigned long long *zero_flag;   // [1] streaming kernel: launch number + 1 once `out` is zeroed
     uint32_t *tile_cnt;    // [T] per-tile split-K arrival counters (zeroed per launch)
     uint32_t *tile_ready;  // [T] per-tile "h published" flags (zeroed per launch)
     uint32_t *tok_bits;    // [B][W] per-token activity bits
@@ -85,6 +88,9 @@ inline Workspace carve_workspace(void *base, int B, int d, int f, int group) {
     };
     uint32_t *sync = (uint32_t *)take(sizeof(uint32_t) * (64 + 2 * (size_t)w.T));
     w.err = sync;
+    w.launch_ctr = sync ? reinterpret_cast<unsigned long long *>(sync + 16) : nullptr;
+    w.zero_flag = sync ? reinterpret_cast<unsigned long long *>(sync + 24) : nullptr;
+    w.grid_bar = sync ? reinterpret_cast<unsigned long long *>(sync + 32) : nullptr;
     w.tile_cnt = sync ? sync + 64 : nullptr;
     w.tile_ready = sync ? sync + 64 + w.T : nullptr;
     w.tok_bits = (uint32_t *)take(sizeof(uint32_t) * (size_t)B * W);

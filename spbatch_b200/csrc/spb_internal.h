@@ -38,8 +38,30 @@ struct FusedGemvArgs {
     int32_t *merge;             // [f] out: union ids
     int32_t *count;             // [1] out: U
     float *out;                 // [B][d], pre-zeroed
+    uint32_t *err;              // [1] sticky device error code
 };
 int launch_fused_gemv(const FusedGemvArgs &a, cudaStream_t st);
+
+// stream_ffn.cu -- single-launch streaming path (B <= 4): union, gather and
+// down projection in one kernel
+struct StreamFfnArgs {
+    const void *wg, *wu, *wd;  // [f][d] rows, format wtype
+    int wtype;
+    const float *x;            // [B][d]
+    const float *idx;          // [B][f] labels, active if > 0
+    int B, d, f, act, per_token;
+    int32_t *merge_out;        // [f] optional: ascending union ids
+    int32_t *count_out;        // [1] optional: union size
+    float *out;                // [B][d]
+    uint32_t *err;             // [1] sticky device error code
+    uint32_t *seg_bits;              // [W] workspace: union words
+    uint32_t *tok_bits;              // [B][W] workspace: token words
+    unsigned long long *grid_bar;    // workspace: grid-barrier arrival counter
+    unsigned long long *launch_ctr;  // workspace: monotonic CTA ticket counter
+    unsigned long long *zero_flag;   // workspace: launch number + 1 once `out` is zeroed
+};
+bool stream_ffn_supported(int wtype, int B, int d);
+int launch_stream_ffn(const StreamFfnArgs &a, cudaStream_t st);
 
 // Drop-in (segment) variants, reference layout: compacted fp32 [B][f] with
 // slot r of token t holding neuron merge_idx[(t/G)*f + r].

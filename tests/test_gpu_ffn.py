@@ -24,9 +24,11 @@ def _run(spb, cuda, wg, wu, wd, x, lab, **kw):
     f = lab.shape[1]
     merge = torch.full((f,), -1, dtype=torch.int32, device=cuda)
     count = torch.zeros(1, dtype=torch.int32, device=cuda)
+    ws = spb.new_workspace(x.shape[0], x.shape[1], f, 0, cuda)
     out = spb.ffn_forward(_dev(wg, cuda), _dev(wu, cuda), _dev(wd, cuda), _dev(x, cuda), _dev(lab, cuda),
-                          merge_idx_out=merge, count_out=count, **kw)
+                          merge_idx_out=merge, count_out=count, workspace=ws, **kw)
     torch.cuda.synchronize()
+    assert _ws_error(ws) == 0, "device wait timed out"
     return out.cpu().numpy(), merge.cpu().numpy(), int(count.cpu()[0])
 
 
@@ -185,3 +187,42 @@ def test_tensor_path_13b_b64(spb, cuda, oracle_mod):
     assert err == 0
     assert U == int((lab > 0).any(0).sum())
     assert_close(out, oracle_mod.ffn(*W, x, lab))
+
+
+@pytest.mark.parametrize("d,f,B,p", [(8192, 1000, 1, 0.1), (8192, 2048, 2, 0.2), (64, 33, 3, 0.5),
+                                     (4096, 4096, 4, 1.0), (2048, 96, 4, 0.0)])
+def test_stream_path_shapes(spb, cuda, oracle_mod, d, f, B, p):
+    """Single-launch streaming path: ragged f, d = 8192 (two chunks per
+    thread), tiny d, a fully dense union (the stage ring wraps many times),
+    and an empty one; no index outputs requested."""
+    import torch
+    rng = np.random.default_rng(d + f + B)
+    wg, wu, wd = _layer(rng, d, f, 0.05)
+    x = rng.standard_normal((B, d)).astype(np.float32)
+    lab = (rng.random((B, f)) < p).astype(np.float32)
+    ws = spb.new_workspace(B, d, f, 0, cuda)
+    out = spb.ffn_forward(_dev(wg, cuda), _dev(wu, cuda), _dev(wd, cuda), _dev(x, cuda), _dev(lab, cuda),
+                          workspace=ws, path=spb.PATH_GEMV)
+    torch.cuda.synchronize()
+    assert_close(out.cpu().numpy(), oracle_mod.ffn(wg, wu, wd, x, lab))
+    assert _ws_error(ws) == 0
+
+
+def test_stream_path_many_calls(spb, cuda, oracle_mod):
+    """The streaming kernel's launch counters are reset by its last CTA, so
+    back-to-back calls on one workspace (no host sync between them) all give
+    the oracle's answer."""
+    import torch
+    rng = np.random.default_rng(11)
+    d, f, B = 1024, 3000, 2
+    wg, wu, wd = _layer(rng, d, f, 0.05)
+    W = [_dev(w, cuda) for w in (wg, wu, wd)]
+    ws = spb.new_workspace(B, d, f, 0, cuda)
+    xs = [rng.standard_normal((B, d)).astype(np.float32) for _ in range(6)]
+    labs = [(rng.random((B, f)) < 0.05 * (i + 1)).astype(np.float32) for i in range(6)]
+    outs = [spb.ffn_forward(*W, _dev(x, cuda), _dev(l, cuda), workspace=ws, path=spb.PATH_GEMV)
+            for x, l in zip(xs, labs)]
+    torch.cuda.synchronize()
+    for x, l, o in zip(xs, labs, outs):
+        assert_close(o.cpu().numpy(), oracle_mod.ffn(wg, wu, wd, x, l))
+    assert _ws_error(ws) == 0
