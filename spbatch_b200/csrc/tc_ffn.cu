@@ -7,18 +7,19 @@
 //
 //  gate/up units   a 128-neuron tile of the batch union (positions
 //                  [128 i, 128 i + 128) of the ascending index list) times a
-//                  K-slice of d.  Each ring stage holds one matrix's gathered
-//                  rows for nkb 64-wide K blocks (a contiguous 128*nkb-byte run
-//                  per row: DRAM efficiency of a row gather grows with the run
-//                  length) plus the matching fp16 activations.  The gathered
-//                  rows arrive by cp.async (a warp copies one row's whole run
-//                  per instruction, so DRAM sees runs, not scattered lines),
-//                  the activations by 2D TMA tiles, all in the 128-byte-
-//                  swizzled K-major layout the MMA reads.  A stage's barrier
-//                  completes on the producers' cp.async arrivals plus the TMA
-//                  transaction bytes, so no producer waits on its own copies.
-//                  Gate
-//                  and up stages alternate; one thread issues
+//                  K-slice of d.  Each ring stage holds one K group: the
+//                  gathered W_gate and W_up rows for nkb 64-wide K blocks (a
+//                  contiguous 128*nkb-byte run per row) plus one copy of the
+//                  matching fp16 activations, shared by both matrices.  The
+//                  gathered rows arrive by cp.async (a warp copies whole row
+//                  runs per instruction), the activations by 2D TMA tiles,
+//                  all in the 128-byte-swizzled K-major layout the MMA reads.
+//                  A stage's barrier completes on the producers' cp.async
+//                  arrivals plus the TMA transaction bytes, so no producer
+//                  waits on its own copies.  The copy rate of the four
+//                  producer warps follows the bytes in flight, so the stage
+//                  size is chosen to keep the most weight bytes in flight in
+//                  the ring (three or more stages).  Per stage one thread issues
 //                  tcgen05.mma.kind::f16 M=128 x N=Np x K=16 into two TMEM
 //                  accumulators.  When several CTAs split a tile's K range,
 //                  each writes its fp32 partials and the last to arrive
@@ -31,11 +32,13 @@
 //                  a contiguous 512-byte run) are the MN-major A operand, h the
 //                  K-major B operand; out^T[2 x 128 x Np] accumulates in TMEM
 //                  and is added into the pre-zeroed output with fp32
-//                  reductions.  Before its first stage each producer waits for
-//                  the ready flags of every gate/up tile the chunk reads.
+//                  reductions.  The W_down rows of a stage are copied as soon
+//                  as its ring slot is free -- they overlap the tail of the
+//                  gate/up phase -- and only the stage's h tile waits for the
+//                  ready flags of the gate/up tiles it reads.
 //
-// Warp roles (288 threads): warps 0-3 epilogue (TMEM lanes 0-127), warps 4-7
-// producers (cp.async + TMA), warp 8 TMEM allocator + MMA issuer.  Waiting
+// Warp roles (416 threads): warps 0-3 epilogue (TMEM lanes 0-127), warps 4-11
+// producers (cp.async + TMA), warp 12 TMEM allocator + MMA issuer.  Waiting
 // threads sleep on the mbarrier (try_wait with a suspend hint) instead of
 // spinning, which would steal shared-memory bandwidth from the producers.
 // Every wait is bounded (2 s of %globaltimer); on timeout the kernel records an
@@ -57,9 +60,14 @@ namespace spb {
 
 using namespace ptx;
 
-constexpr int kTcThreads = 288;
-constexpr int kProducerWarp0 = 4;  // warps 4..7
-constexpr int kMmaWarp = 8;
+// Warp roles: 0-3 epilogue, 4-11 producers, 12 MMA.  The cp.async rate of a
+// warp is bounded by the copies it can keep in flight, so the copy rate of
+// the CTA grows with the number of producer warps (4 warps: ~30 GB/s per SM
+// on a 512-byte row gather, 8 warps: ~50 GB/s).
+constexpr int kProducerWarps = 8;
+constexpr int kProducerWarp0 = 4;
+constexpr int kMmaWarp = kProducerWarp0 + kProducerWarps;
+constexpr int kTcThreads = (kMmaWarp + 1) * 32;
 constexpr int kTileM = 128;          // neurons per gate/up tile, rows per MMA
 constexpr int kDnCols = 256;         // output columns per down item (two M=128 tiles)
 constexpr uint32_t kATile = 16384;   // 128 rows x 128 bytes (one 64-wide K block)
@@ -120,7 +128,7 @@ enum TraceSlot {
     kTrGuMmaDone = 3,    // MMA: last gate/up stage issued + committed
     kTrGuAcc = 4,        // epilogue: gate/up accumulators ready
     kTrGuPublished = 5,  // epilogue: h written / partial handed off
-    kTrFirstFlag = 6,    // producers: every h tile of the down chunk available
+    kTrFirstFlag = 6,    // producers: h tiles of the first down stage available
     kTrDnIssued = 7,     // producers: last down stage issued
     kTrDnAcc = 8,        // epilogue: last down accumulator ready
     kTrEnd = 9,          // before TMEM release
@@ -182,7 +190,7 @@ __device__ __forceinline__ Unit unit_of(const Plan &p, int c, int grid, int u, i
         x.tile = g / p.Sk;
         x.kg0 = ks * p.KG / p.Sk;
         x.kg1 = (ks + 1) * p.KG / p.Sk;
-        x.stages = 2 * (x.kg1 - x.kg0);  // gate and up stages alternate
+        x.stages = x.kg1 - x.kg0;  // one K group (gate + up rows) per stage
         return x;
     }
     if (u == n_gu && c < p.ndn) {
@@ -263,10 +271,12 @@ ffn_tc_kernel(const __grid_constant__ TcMaps maps, const TcArgs a) {
     const int P = a.P, W = a.W, Np = a.Np, nkb = a.nkb, ns = a.ns;
     uint8_t *ring = smem;
     TcCtl *ctl = reinterpret_cast<TcCtl *>(ring + (size_t)P * a.stage_bytes);
-    int *prefix = reinterpret_cast<int *>(ctl + 1);           // [W + 1]
+    // prologue-only tables live in the ring, which no copy touches before the
+    // ids are emitted
+    int *prefix = reinterpret_cast<int *>(ring);               // [W + 1]
     int *wtot = prefix + W + 1;                                // [64]
     uint32_t *bits = reinterpret_cast<uint32_t *>(wtot + 64);  // [W]
-    int *gu_ids = reinterpret_cast<int *>(bits + W);           // [kMaxGuUnits][128]
+    int *gu_ids = reinterpret_cast<int *>(ctl + 1);            // [kMaxGuUnits][128]
     int *dn_ids = gu_ids + kMaxGuUnits * kTileM;               // [max_chunk]
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -274,7 +284,7 @@ ffn_tc_kernel(const __grid_constant__ TcMaps maps, const TcArgs a) {
 
     if (tid == 0) {
         for (int i = 0; i < P; ++i) {
-            mbar_init(&ctl->full[i], 129);  // 128 producer cp.async arrivals + 1 TMA expect_tx arrival
+            mbar_init(&ctl->full[i], kProducerWarps * 32 + 1);  // producer cp.async arrivals + 1 TMA expect_tx arrival
             mbar_init(&ctl->empty[i], 1);
         }
         mbar_init(&ctl->acc_full, 1);
@@ -313,7 +323,7 @@ ffn_tc_kernel(const __grid_constant__ TcMaps maps, const TcArgs a) {
     const uint32_t tmem = ctl->tmem_base;
     if (tid == 0) stamp(a, kTrScanned);
 
-    if (warp >= kProducerWarp0 && warp < kProducerWarp0 + 4) {
+    if (warp >= kProducerWarp0 && warp < kProducerWarp0 + kProducerWarps) {
         // ------------------------------------------------------------ producers
         const int pt = tid - kProducerWarp0 * 32, pw = pt >> 5;
         const bool leader = pt == 0;
@@ -322,19 +332,11 @@ ffn_tc_kernel(const __grid_constant__ TcMaps maps, const TcArgs a) {
         for (int u = 0; u < nunits; ++u) {
             const Unit un = unit_of(pl, c, grid, u, ns);
             bool ok = true;
-            if (un.kind == 1 && un.stages > 0) {
-                // Every gate/up tile this chunk reads h from must be published.
-                // Each producer checks all of them itself: no barrier that a
-                // thread leaving on a timeout could strand the others at.
-                const int t0 = un.P0 / kTileM, t1 = (un.P0 + un.stages * ns - 1) / kTileM;
-                for (int t = t0; t <= t1 && ok; ++t) ok = wait_flag(a.tile_ready + t, ctl, a.err);
-                if (!ok) break;
-                if (leader) stamp(a, kTrFirstFlag);
-            }
+            int flag_next = un.kind == 1 ? un.P0 / kTileM : 0;  // first gate/up tile not yet seen ready
             // CTAs sharing a K range start at different K groups: rows are 8 KB
             // apart, so CTAs stepping through the same column window in lock
             // step would all hit the same few DRAM channels.
-            const int nk = un.kind == 0 ? un.kg1 - un.kg0 : 1;
+            const int nk = un.kind == 0 ? un.kg1 - un.kg0 : 1;  // K groups of the unit
             const int rot = un.kind == 0 && nk > 0 ? (un.tile % nk) : 0;
             for (int st = 0; st < un.stages; ++st, ++s) {
                 const int slot = s % P, round = s / P;
@@ -344,46 +346,62 @@ ffn_tc_kernel(const __grid_constant__ TcMaps maps, const TcArgs a) {
                 const uint32_t sbase = smem_u32(ring + (size_t)slot * a.stage_bytes);
                 if (leader) stage_stamp(a, s, 0);
                 if (un.kind == 0) {
-                    const int kbase = (un.kg0 + ((st >> 1) + rot) % nk) * 64 * nkb;
+                    // one K group: gate and up rows (nkb x 128 B each) + the activations
+                    const int kbase = (un.kg0 + (st + rot) % nk) * 64 * nkb;
                     if (leader) {  // activations: nkb TMA tiles of 64 columns x Np rows
                         mbar_arrive_expect_tx(bar, (uint32_t)nkb * Np * 128);
                         for (int kbl = 0; kbl < nkb; ++kbl)
-                            tma_load_2d(sbase + nkb * kATile + kbl * Np * 128, &maps.x, bar, kbase + kbl * 64, 0);
+                            tma_load_2d(sbase + 2 * nkb * kATile + kbl * Np * 128, &maps.x, bar, kbase + kbl * 64, 0);
                     }
-                    // weights: 128 rows x (nkb x 128 B); each warp instruction copies whole row runs
-                    const __half *w = ((st & 1) ? a.wu : a.wg) + kbase;
+                    // weights: 128 rows x (nkb x 128 B) per matrix; each warp
+                    // instruction copies whole row runs
                     const int cpr = nkb * 8;    // 16-byte chunks per row run
                     const int rpw = 32 / cpr;   // rows per warp instruction
                     const int ch = lane & (cpr - 1), kbl = ch >> 3, cc = ch & 7;
                     if (copy_w) {
-                        const __half *wl = w + ch * 8;
-                        const uint32_t dl = sbase + kbl * kATile + (uint32_t)cc * 16;
-                        for (int r = pw * rpw + lane / cpr; r < 128; r += 4 * rpw) {
-                            const int j = gu_ids[u * kTileM + r];
-                            // padding rows past the union copy row 0: the epilogue
-                            // zeroes h for them, so their products are never used
-                            cp_async16_full((dl + r * 128) ^ ((uint32_t)(r & 7) << 4),
-                                            wl + (int64_t)(j < a.f ? j : 0) * a.d);
+#pragma unroll
+                        for (int m = 0; m < 2; ++m) {
+                            const __half *wl = (m ? a.wu : a.wg) + kbase + ch * 8;
+                            const uint32_t dl = sbase + (m * nkb + kbl) * kATile + (uint32_t)cc * 16;
+                            for (int r = pw * rpw + lane / cpr; r < 128; r += kProducerWarps * rpw) {
+                                const int j = gu_ids[u * kTileM + r];
+                                // padding rows past the union copy row 0: the epilogue
+                                // zeroes h for them, so their products are never used
+                                cp_async16_full((dl + r * 128) ^ ((uint32_t)(r & 7) << 4),
+                                                wl + (int64_t)(j < a.f ? j : 0) * a.d);
+                            }
                         }
                     }
                 } else {
                     const int p0s = un.P0 + st * ns;
-                    if (leader) {  // h: ns/64 TMA tiles of 64 neurons x Np tokens
-                        mbar_arrive_expect_tx(bar, (uint32_t)(ns / 64) * Np * 128);
-                        for (int kbl = 0; kbl < ns / 64; ++kbl)
-                            tma_load_2d(sbase + (uint32_t)ns * 512 + kbl * Np * 128, &maps.h, bar, p0s + kbl * 64, 0);
-                    }
-                    // W_down rows as the MN-major operand: ns neurons x 256 columns (32 chunks), one row per warp
+                    // W_down rows as the MN-major operand: ns neurons x 256
+                    // columns (32 chunks), one row per warp.  They do not depend
+                    // on the gate/up phase, so they are copied at once; only h
+                    // waits for its tiles below.
                     const int m0 = un.mt * kDnCols;
                     const uint32_t lbo = (uint32_t)(ns / 8) * 1024;
                     const int mb = lane >> 3, cc = lane & 7;
                     if (copy_w) {
-                        for (int kk = pw; kk < ns; kk += 4) {
+                        for (int kk = pw; kk < ns; kk += kProducerWarps) {
                             const int j = dn_ids[(p0s - un.P0) + kk];
                             const int kg = kk >> 3, kr = kk & 7;
                             cp_async16(sbase + mb * lbo + kg * 1024 + kr * 128 + ((cc ^ kr) << 4),
                                        a.wd + (int64_t)(j < a.f ? j : 0) * a.d + m0 + lane * 8, j < a.f ? 16u : 0u);
                         }
+                    }
+                    if (leader) {
+                        // h of this stage's neurons: wait for the gate/up tiles
+                        // that hold them (published by other CTAs), then TMA
+                        // ns/64 tiles of 64 neurons x Np tokens.
+                        const int t1 = (min(p0s + ns, un.P1) - 1) / kTileM;
+                        for (; flag_next <= t1 && ok; ++flag_next) ok = wait_flag(a.tile_ready + flag_next, ctl, a.err);
+                        if (st == 0) stamp(a, kTrFirstFlag);
+                        // the h stores were made through the generic proxy;
+                        // the TMA below reads through the async proxy
+                        asm volatile("fence.proxy.async.global;" ::: "memory");
+                        mbar_arrive_expect_tx(bar, (uint32_t)(ns / 64) * Np * 128);
+                        for (int kbl = 0; kbl < ns / 64; ++kbl)
+                            tma_load_2d(sbase + (uint32_t)ns * 512 + kbl * Np * 128, &maps.h, bar, p0s + kbl * 64, 0);
                     }
                 }
                 cp_async_mbar_arrive(bar);
@@ -418,14 +436,18 @@ ffn_tc_kernel(const __grid_constant__ TcMaps maps, const TcArgs a) {
                     tc_fence_after();
                     const uint32_t sbase = smem_u32(ring + (size_t)slot * a.stage_bytes);
                     if (do_mma && un.kind == 0) {
-                        const uint32_t dcol = tmem + (st & 1) * Np;  // gate or up accumulator
-                        const uint32_t xoff = nkb * kATile;
+                        // gate rows -> TMEM columns [0, Np), up rows -> [Np, 2 Np)
+                        const uint32_t xoff = 2 * nkb * kATile;
                         for (int kbl = 0; kbl < nkb; ++kbl) {
 #pragma unroll
                             for (int k4 = 0; k4 < 4; ++k4) {
-                                const uint64_t ad = desc_sw128(sbase + kbl * kATile + k4 * 32, 16, 1024);
                                 const uint64_t bd = desc_sw128(sbase + xoff + kbl * Np * 128 + k4 * 32, 16, 1024);
-                                mma_f16(dcol, ad, bd, id_gu, (st > 1 || kbl > 0 || k4 > 0) ? 1u : 0u);
+                                const uint32_t acc = (st > 0 || kbl > 0 || k4 > 0) ? 1u : 0u;
+#pragma unroll
+                                for (int m = 0; m < 2; ++m) {
+                                    const uint64_t ad = desc_sw128(sbase + (m * nkb + kbl) * kATile + k4 * 32, 16, 1024);
+                                    mma_f16(tmem + m * Np, ad, bd, id_gu, acc);
+                                }
                             }
                         }
                     } else if (do_mma) {
@@ -632,8 +654,8 @@ int tensor_map(const void *ptr, uint64_t cols, uint64_t rows, uint32_t box_rows,
 
 }  // namespace
 
-// Stage geometry: the longest row run (K blocks per gate/up stage) that still
-// leaves `want` ring stages; the down stage uses the same slot.
+// Stage geometry: K blocks per gate/up stage, neurons per down stage and ring
+// depth; both kinds of stage share the ring slots.
 struct Geometry {
     int nkb, ns, P;
     uint32_t stage_bytes;
@@ -641,28 +663,30 @@ struct Geometry {
 };
 
 static Geometry pick_geometry(int Np, int W, int max_chunk, int d) {
-    const size_t fixed = sizeof(TcCtl) + sizeof(int) * (W + 1 + 64) + sizeof(uint32_t) * W +
-                         sizeof(int) * (kMaxGuUnits * kTileM + max_chunk) + 1024 + 64;
+    const size_t fixed = sizeof(TcCtl) + sizeof(int) * (kMaxGuUnits * kTileM + max_chunk) + 1024 + 64;
+    const size_t prologue = sizeof(int) * (W + 1 + 64) + sizeof(uint32_t) * W;  // in the ring
     const size_t budget = 227 * 1024;
     const char *env = getenv("SPB_TC_NKB");
     const int forced = env ? atoi(env) : 0;
-    const char *envp = getenv("SPB_TC_MINP");
-    const int want_p = envp ? atoi(envp) : 2;
+    // The producer warps' copy rate follows the weight bytes in flight: maximise (P - 1) x the smaller of the gate/up and down
+    // stages' weight bytes; prefer longer row runs on ties.
     Geometry best{0, 0, 0, 0, 0};
-    for (int pass = 0; pass < 2 && best.P == 0; ++pass) {
-        for (int nkb = 4; nkb >= 1; --nkb) {
-            if (forced && nkb != forced) continue;
-            if ((d / 64) % nkb) continue;
-            const uint32_t gu = (uint32_t)nkb * (kATile + (uint32_t)Np * 128);
-            int ns = 128;
-            if ((uint32_t)ns * 512 + 2u * Np * 128 > gu) ns = 64;
+    size_t best_score = 0;
+    for (int nkb = 4; nkb >= 1; --nkb) {
+        if (forced && nkb != forced) continue;
+        if ((d / 64) % nkb) continue;
+        for (int ns = 128; ns >= 64; ns -= 64) {
+            const uint32_t gu = (uint32_t)nkb * (2 * kATile + (uint32_t)Np * 128);
             const uint32_t dn = (uint32_t)ns * 512 + (uint32_t)(ns / 64) * Np * 128;
             const uint32_t stage = ((gu > dn ? gu : dn) + 1023) & ~1023u;
-            if (fixed + 2 * (size_t)stage > budget) continue;
+            if (fixed + 2 * (size_t)stage > budget || 2 * (size_t)stage < prologue) continue;
             const int P = (int)std::min<size_t>((budget - fixed) / stage, kMaxStages);
-            if (P >= (pass == 0 ? want_p : 2)) {
+            const size_t w_gu = (size_t)nkb * 2 * kATile, w_dn = (size_t)ns * 512;
+            // rank: the longer row run, then the weight bytes in flight
+            const size_t score = ((size_t)nkb << 40) + (size_t)(P - 1) * std::min(w_gu, w_dn);
+            if (score > best_score) {
+                best_score = score;
                 best = Geometry{nkb, ns, P, stage, fixed + (size_t)P * stage};
-                break;
             }
         }
     }

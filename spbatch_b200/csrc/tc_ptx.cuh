@@ -90,6 +90,25 @@ __device__ __forceinline__ void cp_async16_full(uint32_t dst, const void *src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
 }
 
+// cp_async16_full with an L2 cache-eviction policy (from createpolicy).
+__device__ __forceinline__ void cp_async16_hint(uint32_t dst, const void *src, uint64_t policy) {
+    asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "l"(policy)
+                 : "memory");
+}
+
+// L2 policy under which the lines a load brings in are the first to be evicted.
+__device__ __forceinline__ uint64_t policy_evict_first() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
+// Asks the TMA unit to pull `bytes` (multiple of 16, 16-byte aligned) of
+// global memory into L2; nothing waits for it.
+__device__ __forceinline__ void bulk_prefetch_l2(const void *src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 
 // cp.async.wait_group takes an immediate; dispatch the small runtime range.
