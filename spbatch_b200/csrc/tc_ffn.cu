@@ -37,8 +37,8 @@
 //                  gate/up phase -- and only the stage's h tile waits for the
 //                  ready flags of the gate/up tiles it reads.
 //
-// Warp roles (416 threads): warps 0-3 epilogue (TMEM lanes 0-127), warps 4-11
-// producers (cp.async + TMA), warp 12 TMEM allocator + MMA issuer.  Waiting
+// Warp roles (544 threads): warps 0-3 epilogue (TMEM lanes 0-127), warps 4-15
+// producers (cp.async + TMA), warp 16 TMEM allocator + MMA issuer.  Waiting
 // threads sleep on the mbarrier (try_wait with a suspend hint) instead of
 // spinning, which would steal shared-memory bandwidth from the producers.
 // Every wait is bounded (2 s of %globaltimer); on timeout the kernel records an
@@ -60,11 +60,11 @@ namespace spb {
 
 using namespace ptx;
 
-// Warp roles: 0-3 epilogue, 4-11 producers, 12 MMA.  The cp.async rate of a
+// Warp roles: 0-3 epilogue, 4-15 producers, 16 MMA.  The cp.async rate of a
 // warp is bounded by the copies it can keep in flight, so the copy rate of
 // the CTA grows with the number of producer warps (4 warps: ~30 GB/s per SM
-// on a 512-byte row gather, 8 warps: ~50 GB/s).
-constexpr int kProducerWarps = 8;
+// on a 512-byte row gather, 8 warps: ~50 GB/s in isolation).
+constexpr int kProducerWarps = 12;
 constexpr int kProducerWarp0 = 4;
 constexpr int kMmaWarp = kProducerWarp0 + kProducerWarps;
 constexpr int kTcThreads = (kMmaWarp + 1) * 32;
