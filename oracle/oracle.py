@@ -36,6 +36,8 @@ def build(ref: bool = False) -> None:
     subprocess.check_call(["make", "-s", "-C", HERE, "all"])
     if ref and os.path.isdir("/root/reference/cuda"):
         subprocess.check_call(["make", "-s", "-C", HERE, "ref"])
+        # the reference's spmm_test driver against this library and its own
+        subprocess.check_call(["make", "-s", "-C", HERE, "drivers"])
 
 
 def lib():

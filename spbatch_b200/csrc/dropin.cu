@@ -45,6 +45,22 @@ void *scratch(int slot, size_t bytes) {
     return s.ptr;
 }
 
+// Sticky device error word for the drop-in kernels' bounded waits (the
+// reference API returns void, so it is only there for inspection).
+uint32_t *err_word() {
+    static std::mutex mu;
+    static std::unordered_map<int, uint32_t *> table;
+    int dev = 0;
+    CUDA_CHECK(cudaGetDevice(&dev));
+    std::lock_guard<std::mutex> lk(mu);
+    uint32_t *&p = table[dev];
+    if (!p) {
+        CUDA_CHECK(cudaMalloc(&p, 256));
+        CUDA_CHECK(cudaMemset(p, 0, 256));
+    }
+    return p;
+}
+
 constexpr int kEw = 256;
 
 __global__ void f32_to_f16_kernel(const float *__restrict__ x, __half *__restrict__ y, int k) {
@@ -254,16 +270,27 @@ void get_idx_cuda(const float *idx, int *merge_idx, int *act_neurons_device, con
 void up_mul_mat_cuda_sparse(const half *weight, const float *input, float *dst, int *merge_idx, const int M,
                             const int N, const int K, const int *act_neurons_device, cudaStream_t stream) {
     if (N <= 0 || M <= 0) return;
-    DROPIN_OK(launch_dropin_up(weight, nullptr, input, dst, nullptr, merge_idx, act_neurons_device,
-                               (N / SPARSITY_GROUP_SIZE) * SPARSITY_GROUP_SIZE, K, M, SPARSITY_GROUP_SIZE, stream));
+    const int Bu = (N / SPARSITY_GROUP_SIZE) * SPARSITY_GROUP_SIZE;
+    if (dropin_up_stream_supported(Bu, K, SPARSITY_GROUP_SIZE)) {
+        DROPIN_OK(launch_dropin_up_stream(weight, nullptr, input, dst, nullptr, merge_idx, act_neurons_device, Bu, K,
+                                          M, SPARSITY_GROUP_SIZE, err_word(), stream));
+        return;
+    }
+    DROPIN_OK(launch_dropin_up(weight, nullptr, input, dst, nullptr, merge_idx, act_neurons_device, Bu, K, M,
+                               SPARSITY_GROUP_SIZE, stream));
 }
 
 void gate_and_up_mul_mat_cuda_sparse(const half *gate_w, const half *up_w, const float *input, float *gate_dst,
                                      float *up_dst, int *merge_idx, const int M, const int N, const int K,
                                      const int *act_neurons_device, cudaStream_t stream0, cudaStream_t stream1) {
     if (N <= 0 || M <= 0) return;
-    DROPIN_OK(launch_dropin_up(gate_w, up_w, input, gate_dst, up_dst, merge_idx, act_neurons_device,
-                               (N / SPARSITY_GROUP_SIZE) * SPARSITY_GROUP_SIZE, K, M, SPARSITY_GROUP_SIZE, stream0));
+    const int Bu = (N / SPARSITY_GROUP_SIZE) * SPARSITY_GROUP_SIZE;
+    if (dropin_up_stream_supported(Bu, K, SPARSITY_GROUP_SIZE))
+        DROPIN_OK(launch_dropin_up_stream(gate_w, up_w, input, gate_dst, up_dst, merge_idx, act_neurons_device, Bu,
+                                          K, M, SPARSITY_GROUP_SIZE, err_word(), stream0));
+    else
+        DROPIN_OK(launch_dropin_up(gate_w, up_w, input, gate_dst, up_dst, merge_idx, act_neurons_device, Bu, K, M,
+                                   SPARSITY_GROUP_SIZE, stream0));
     if (stream1 != stream0) {
         // The reference computes up on stream1; order stream1 after the fused
         // launch so work queued there sees up_dst.

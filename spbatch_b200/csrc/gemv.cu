@@ -88,12 +88,31 @@ __device__ __forceinline__ void row_dot2(const __half *__restrict__ rg, const __
 
 // Loads tokens [t0, t0 + NT) of x (rows of d fp32) into shared memory rounded
 // to fp16 (the reference converts x to fp16 before its products,
-// cuda/kernel.cu:978); tokens >= B are zero.
+// cuda/kernel.cu:978); tokens >= B are zero.  float4 loads, eight in flight
+// per thread (d % 4 == 0: rows stay 16-byte aligned).
 template <int NT>
 __device__ __forceinline__ void load_x_rounded(const float *__restrict__ x, int B, int t0, int d, float *xs) {
-    for (int i = threadIdx.x; i < NT * d; i += blockDim.x) {
-        const int t = i / d, k = i - t * d;
-        xs[i] = (t0 + t < B) ? __half2float(__float2half_rn(x[(int64_t)(t0 + t) * d + k])) : 0.0f;
+    const int d4 = d >> 2, n4 = NT * d4;
+    constexpr int kInFlight = 8;
+    for (int base = threadIdx.x; base < n4; base += kInFlight * blockDim.x) {
+        float4 v[kInFlight];
+#pragma unroll
+        for (int u = 0; u < kInFlight; ++u) {
+            const int i = base + u * blockDim.x;
+            const int t = i / d4;
+            v[u] = (i < n4 && t0 + t < B)
+                       ? __ldg(reinterpret_cast<const float4 *>(x + (int64_t)(t0 + t) * d) + (i - t * d4))
+                       : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int u = 0; u < kInFlight; ++u) {
+            const int i = base + u * blockDim.x;
+            if (i < n4) {
+                const float4 r = make_float4(__half2float(__float2half_rn(v[u].x)), __half2float(__float2half_rn(v[u].y)),
+                                             __half2float(__float2half_rn(v[u].z)), __half2float(__float2half_rn(v[u].w)));
+                reinterpret_cast<float4 *>(xs)[i] = r;
+            }
+        }
     }
 }
 

@@ -61,6 +61,11 @@ struct StreamFfnArgs {
     unsigned long long *zero_flag;   // workspace: launch number + 1 once `out` is zeroed
 };
 bool stream_ffn_supported(int wtype, int B, int d);
+// drop-in up projection on the bulk-copy streaming design (fp16, d <= 4096)
+bool dropin_up_stream_supported(int B, int d, int G);
+int launch_dropin_up_stream(const __half *wg, const __half *wu, const float *x, float *gate_dst, float *up_dst,
+                            const int32_t *merge_idx, const int32_t *act_cum, int B, int d, int f, int G,
+                            uint32_t *err, cudaStream_t st);
 int launch_stream_ffn(const StreamFfnArgs &a, cudaStream_t st);
 
 // Drop-in (segment) variants, reference layout: compacted fp32 [B][f] with

@@ -712,6 +712,179 @@ int launch_sf_wt(const StreamFfnArgs &fa, cudaStream_t st) {
     return launch_sf<2, WT, 2>(fa, st);
 }
 
+
+// ---- drop-in up projection (group-union semantics) --------------------------
+//
+// up_mul_mat_cuda_sparse / gate_and_up_mul_mat_cuda_sparse (cuda/kernel.cu:
+// 595-704, 971-1010) compute, for each group of G <= 8 tokens, the products of
+// the group's compacted neuron list with the group's tokens, written
+// compacted: dst[t][r] = W[merge_idx[g][r]] . fp16(x[t]).  Here the CTAs are
+// split evenly over the groups and each takes an equal share of its group's
+// list, so the group's activations stay in registers (fp16 pairs) for the
+// whole launch.  Rows stream through the same bulk-copy ring as the fused
+// kernel; per group of 4 (up) or 2 (gate + up) neurons the 32 partial sums
+// are reduce-scattered across the warp, summed over the warps in fixed order
+// and written by warp 0.
+struct DropUpArgs {
+    const uint8_t *wg, *wu;     // [f][d] fp16 rows (wu null: up only)
+    const float *x;             // [B][d]
+    float *gdst, *udst;         // [B][f] compacted
+    const int32_t *merge_idx;   // [S][f]
+    const int32_t *act_cum;     // [S] cumulative counts
+    int B, d, f, G, S, stages, cap, rb, stage_bytes;
+    int off_nid, off_red, off_stage;
+    uint32_t *err;
+};
+
+template <int NMAT>
+__global__ void __launch_bounds__(kSfThreads, 1) dropin_up_stream_kernel(const DropUpArgs a) {
+    extern __shared__ __align__(1024) uint8_t smem[];
+    SfCtl *ctl = reinterpret_cast<SfCtl *>(smem);
+    int *nid = reinterpret_cast<int *>(smem + a.off_nid);
+    float *red = reinterpret_cast<float *>(smem + a.off_red);  // [2][kSfWarps][32]
+    uint8_t *stage = smem + a.off_stage;
+    constexpr int NT = 8;                 // tokens per group (G <= 8)
+    constexpr int GN = NMAT == 1 ? 4 : 2;  // neurons per reduction barrier
+    constexpr int V = GN * NT * NMAT;      // = 32 values per group of neurons
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int S = a.stages;
+
+    // this CTA's group and share of the group's list
+    const int per = gridDim.x / a.S;  // CTAs per group (the host keeps grid >= S)
+    const int sg = blockIdx.x / per, local = blockIdx.x - sg * per;
+    if (sg >= a.S) return;
+    const int n_s = a.act_cum[sg] - (sg > 0 ? a.act_cum[sg - 1] : 0);
+    const int p0 = (int)((int64_t)n_s * local / per), p1 = (int)((int64_t)n_s * (local + 1) / per);
+    const int n = p1 - p0;
+    const int t0 = sg * a.G, tend = min(a.B, t0 + a.G);
+
+    if (tid == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&ctl->full[s], 1);
+            mbar_init(&ctl->empty[s], kSfWarps);
+        }
+        ctl->abort = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    for (int i = tid; i < n; i += kSfThreads) nid[i] = a.merge_idx[(int64_t)sg * a.f + p0 + i];
+    __syncthreads();
+
+    if (warp == kSfWarps) {
+        if (lane == 0) {
+            int s = 0;
+            uint32_t ph = 0;
+            for (int i = 0; i < n; ++i) {
+                if (i >= S && !sf_wait(&ctl->empty[s], ph ^ 1u, ctl, a.err, kErrSfEmpty)) break;
+                const int64_t off = (int64_t)nid[i] * a.rb;
+                uint8_t *dst = stage + (size_t)s * a.stage_bytes;
+                mbar_arrive_expect_tx(&ctl->full[s], (uint32_t)a.stage_bytes);
+                bulk_copy(smem_u32(dst), a.wg + off, a.rb, &ctl->full[s]);
+                if (NMAT == 2) bulk_copy(smem_u32(dst + a.rb), a.wu + off, a.rb, &ctl->full[s]);
+                if (++s == S) {
+                    s = 0;
+                    ph ^= 1u;
+                }
+            }
+        }
+        return;
+    }
+
+    // consumers: this thread's 8-element chunk of d for the group's tokens
+    const int c = tid;  // d <= 4096: one chunk per thread
+    uint32_t xh[NT][4];
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+        float4 v0 = make_float4(0.f, 0.f, 0.f, 0.f), v1 = v0;
+        if (c < (a.d >> 3) && t0 + t < tend) {
+            const float4 *xp = reinterpret_cast<const float4 *>(a.x + (int64_t)(t0 + t) * a.d + c * 8);
+            v0 = __ldg(xp);
+            v1 = __ldg(xp + 1);
+        }
+        const float v[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const __half2 p = __floats2half2_rn(v[2 * q], v[2 * q + 1]);
+            xh[t][q] = *reinterpret_cast<const uint32_t *>(&p);
+        }
+    }
+    const bool own = c < (a.d >> 3);
+    int s_next = 0;
+    uint32_t ph_next = 0;
+    bool failed = false;
+    for (int i0 = 0, grp = 0; i0 < n; i0 += GN, ++grp) {
+        int st[GN];
+        float part[V];
+#pragma unroll
+        for (int v = 0; v < V; ++v) part[v] = 0.0f;
+#pragma unroll
+        for (int g = 0; g < GN; ++g) {
+            st[g] = s_next;
+            if (i0 + g < n) {
+                const int s = s_next;
+                if (!failed && !sf_wait(&ctl->full[s], ph_next, ctl, a.err, kErrSfFull)) failed = true;
+                if (++s_next == S) {
+                    s_next = 0;
+                    ph_next ^= 1u;
+                }
+                if (own) {
+                    const uint8_t *row = stage + (size_t)s * a.stage_bytes;
+#pragma unroll
+                    for (int m = 0; m < NMAT; ++m) {
+                        const uint4 w = *reinterpret_cast<const uint4 *>(row + m * a.rb + (size_t)c * 16);
+#pragma unroll
+                        for (int t = 0; t < NT; ++t)
+                            part[(m * GN + g) * NT + t] = dot8_f16(w, xh[t], part[(m * GN + g) * NT + t]);
+                    }
+                }
+            }
+        }
+        const float mine = ReduceScatter<V, 16>::run(part, lane);  // lane l: value l
+        float *rbuf = red + (size_t)(grp & 1) * kSfWarps * V;
+        rbuf[warp * V + lane] = mine;
+        named_bar(1, kSfConsumers);
+        // the rows of this group are no longer needed
+#pragma unroll
+        for (int g = 0; g < GN; ++g)
+            if (i0 + g < n && lane == 0) mbar_arrive(&ctl->empty[st[g]]);
+        if (warp == 0) {
+            float tot = 0.0f;
+#pragma unroll
+            for (int w = 0; w < kSfWarps; ++w) tot += rbuf[w * V + lane];
+            const int m = lane / (GN * NT), g = (lane / NT) % GN, t = lane % NT;
+            if (i0 + g < n && t0 + t < tend) {
+                float *dst = m ? a.udst : a.gdst;
+                dst[(int64_t)(t0 + t) * a.f + p0 + i0 + g] = tot;
+            }
+        }
+    }
+}
+
+template <int NMAT>
+int launch_dropin_up_stream_t(const DropUpArgs &in, cudaStream_t st) {
+    DropUpArgs a = in;
+    const int grid = num_sms();
+    const int per = grid / a.S;
+    a.cap = a.f / per + 2;
+    a.rb = a.d * 2;
+    a.stage_bytes = NMAT * a.rb;
+    size_t off = align_up(sizeof(SfCtl), 16);
+    a.off_nid = (int)off;
+    off = align_up(off + sizeof(int) * a.cap, 16);
+    a.off_red = (int)off;
+    off = align_up(off + sizeof(float) * 2 * kSfWarps * 32, 1024);
+    a.off_stage = (int)off;
+    int S = (int)((kSfSmemLimit - off) / (size_t)a.stage_bytes);
+    if (S > kSfMaxStages) S = kSfMaxStages;
+    if (S < 2) return fail(SPB_ERR_UNSUPPORTED, "drop-in up: rows too long for shared-memory staging");
+    a.stages = S;
+    const size_t smem = off + (size_t)S * a.stage_bytes;
+    auto kern = dropin_up_stream_kernel<NMAT>;
+    if (int rc = ensure_smem((const void *)kern, smem)) return rc;
+    kern<<<per * a.S, kSfThreads, smem, st>>>(a);
+    SPB_LAUNCH_CHECK("dropin_up_stream_kernel");
+    return SPB_OK;
+}
+
 }  // namespace
 
 bool stream_ffn_supported(int wtype, int B, int d) {
@@ -722,6 +895,31 @@ bool stream_ffn_supported(int wtype, int B, int d) {
                        : wtype == SPB_W_Q8_0 ? row_bytes_of<SPB_W_Q8_0>(d)
                                              : row_bytes_of<SPB_W_Q4_0>(d);
     return rb % 16 == 0;
+}
+
+bool dropin_up_stream_supported(int B, int d, int G) {
+    const int S = (B + G - 1) / G;
+    return G >= 1 && G <= 8 && d % 64 == 0 && d <= 4096 && S <= num_sms();
+}
+
+int launch_dropin_up_stream(const __half *wg, const __half *wu, const float *x, float *gate_dst, float *up_dst,
+                            const int32_t *merge_idx, const int32_t *act_cum, int B, int d, int f, int G,
+                            uint32_t *err, cudaStream_t st) {
+    DropUpArgs a{};
+    a.wg = reinterpret_cast<const uint8_t *>(wg);
+    a.wu = reinterpret_cast<const uint8_t *>(wu);
+    a.x = x;
+    a.gdst = gate_dst;
+    a.udst = up_dst;
+    a.merge_idx = merge_idx;
+    a.act_cum = act_cum;
+    a.B = B;
+    a.d = d;
+    a.f = f;
+    a.G = G;
+    a.S = (B + G - 1) / G;
+    a.err = err;
+    return wu ? launch_dropin_up_stream_t<2>(a, st) : launch_dropin_up_stream_t<1>(a, st);
 }
 
 int launch_stream_ffn(const StreamFfnArgs &a, cudaStream_t st) {
