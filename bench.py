@@ -4,6 +4,11 @@ fraction of the HBM roofline on active-weight bytes).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                     [--model 7b] [--batch B] [--activity 0.10] [--path auto]
+                    [--wtype f16|q8_0|q4_0] [--predictor] [--shard] [--config 1..5]
+
+--config N applies BASELINE.json configuration N (1: 7B B=1 with the
+predictor, 2: 7B B=32 -- the default --, 3: 13B B=64 8% with a predictor per
+layer over 40 layers, 4: 7B Q4_0, 5: 70B neuron-sharded); explicit flags win.
 
 A step is one sparse FFN layer (union -> gathered gate/up -> ReLU*up ->
 gathered down) over one batch of B tokens.  Steps rotate over L distinct
@@ -55,7 +60,29 @@ def parse():
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--shard", action="store_true",
                     help="shard the layer's neurons across the torchrun ranks (config 5) instead of replicas")
-    return ap.parse_args()
+    ap.add_argument("--wtype", choices=["f16", "q8_0", "q4_0"], default="f16",
+                    help="weight format (config 4: ggml block quantisation of fp32 N(0, 0.02^2) weights)")
+    ap.add_argument("--predictor", action="store_true",
+                    help="run the DejaVu predictor (P1 [1024][d], P2 [f][1024], top-k per token) ahead of each "
+                         "layer; its labels feed the FFN and its bytes count in the roofline (configs 1 and 3)")
+    ap.add_argument("--config", type=int, default=0, choices=[0, 1, 2, 3, 4, 5],
+                    help="BASELINE.json configuration preset (0: the flags as given)")
+    a = ap.parse_args()
+    presets = {
+        1: dict(model="7b", batch=1, activity=0.10, predictor=True),
+        2: dict(model="7b", batch=32, activity=0.10),
+        3: dict(model="13b", batch=64, activity=0.08, predictor=True, layers=40),
+        4: dict(model="7b", batch=32, activity=0.10, wtype="q4_0"),
+        5: dict(model="70b", batch=32, activity=0.10, shard=True),
+    }
+    given = {k.lstrip("-").replace("-", "_") for k in sys.argv[1:] if k.startswith("--")}
+    for k, v in presets.get(a.config, {}).items():
+        if k not in given:
+            setattr(a, k, v)
+    return a
+
+
+PRED_RANK = 1024  # DejaVu predictor rank D (BASELINE configs 1 and 3)
 
 
 def hbm_peak():
@@ -68,8 +95,10 @@ def hbm_peak():
 
 
 def workload_name(a, U):
-    return (f"{a.model} sparse FFN layer (ReLU-gated SwiGLU), B={a.batch}, fp16 weights, "
-            f"{a.activity:.0%} per-token activity Zipf(0.8), union U~{U}")
+    wt = {"f16": "fp16 weights", "q8_0": "Q8_0 weights", "q4_0": "Q4_0 weights"}[a.wtype]
+    act = (f"{a.activity:.0%} per-token activity from the DejaVu predictor (top-k, run ahead of the layer)"
+           if a.predictor else f"{a.activity:.0%} per-token activity Zipf(0.8)")
+    return f"{a.model} sparse FFN layer (ReLU-gated SwiGLU), B={a.batch}, {wt}, {act}, union U~{U}"
 
 
 def dist_env():
@@ -141,19 +170,44 @@ def make_layers(a, L, device, rank, world=1):
     k = int(round(a.activity * f))
     seed = 0 if a.shard else rank
     f0, f1 = shard_range(f, world, rank) if a.shard else (0, f)
+    import spbatch_b200 as spb
     gen = torch.Generator(device=device)
     gen.manual_seed(1234 + rank)
+    quant = None
+    if a.wtype != "f16":
+        # ggml block quantisation of one fp32 N(0, 0.02^2) set (host quantiser,
+        # byte-identical to the oracle); every layer gets its own copy, so the
+        # rotation still touches distinct addresses
+        wt = spb.W_Q8_0 if a.wtype == "q8_0" else spb.W_Q4_0
+        quant = [torch.from_numpy(spb.quantize((torch.randn((f1 - f0, d), generator=gen, device=device) * 0.02)
+                                               .cpu().numpy(), wt)).to(device) for _ in range(3)]
+    pws = spb.predict_workspace(a.batch, PRED_RANK, f1 - f0, device) if a.predictor else None
     layers = []
     for l in range(L):
-        W = [(torch.randn((f1 - f0, d), generator=gen, device=device) * 0.02).half() for _ in range(3)]
-        lab_full = zipf_active_labels(a.batch, f, k, seed=seed, layer=l)
-        lab_np = np.ascontiguousarray(lab_full[:, f0:f1])
+        if quant is not None:
+            W = [q.clone() for q in quant]
+        else:
+            W = [(torch.randn((f1 - f0, d), generator=gen, device=device) * 0.02).half() for _ in range(3)]
         x_np = np.random.default_rng([seed, l]).standard_normal((a.batch, d)).astype(np.float32)
-        layers.append(dict(i=l, W=W, lab_np=lab_np, x_np=x_np, U=int((lab_np > 0).any(0).sum()),
-                           U_full=int((lab_full > 0).any(0).sum()),
-                           lab=torch.from_numpy(lab_np).to(device), x=torch.from_numpy(x_np).to(device),
+        x = torch.from_numpy(x_np).to(device)
+        P = None
+        if a.predictor:
+            # DejaVu low-rank predictor: P1 [D][d] ~ N(0, 1/d), P2 [f][D] ~ N(0, 1/D); its per-token
+            # top-k labels drive this layer
+            P = [(torch.randn((PRED_RANK, d), generator=gen, device=device) / math.sqrt(d)).half(),
+                 (torch.randn((f1 - f0, PRED_RANK), generator=gen, device=device) / math.sqrt(PRED_RANK)).half()]
+            lab = spb.predict(P[0], P[1], x, k=k, workspace=pws)
+            torch.cuda.synchronize()
+            lab_np = lab.cpu().numpy()
+            lab_full = lab_np
+        else:
+            lab_full = zipf_active_labels(a.batch, f, k, seed=seed, layer=l)
+            lab_np = np.ascontiguousarray(lab_full[:, f0:f1])
+            lab = torch.from_numpy(lab_np).to(device)
+        layers.append(dict(i=l, W=W, P=P, lab_np=lab_np, x_np=x_np, U=int((lab_np > 0).any(0).sum()),
+                           U_full=int((lab_full > 0).any(0).sum()), lab=lab, x=x,
                            out=torch.empty((a.batch, d), device=device)))
-    return d, f1 - f0, k, layers
+    return d, f1 - f0, k, layers, pws
 
 
 def run_ours(a):
@@ -171,20 +225,28 @@ def run_ours(a):
 
     from spbatch_b200.workload import SHAPES
     d0, f0 = SHAPES[a.model]["d"], SHAPES[a.model]["f"]
-    est = active_bytes(d0, min(f0, int(a.activity * f0 * min(a.batch, 8))), a.batch)
+    wb = {"f16": 2.0, "q8_0": 34 / 32, "q4_0": 18 / 32}[a.wtype]
+    est = active_bytes(d0, min(f0, int(a.activity * f0 * min(a.batch, 8))), a.batch, wb,
+                       (d0 * PRED_RANK + PRED_RANK * f0) * 2 if a.predictor else 0)
     if a.shard:
         est /= ws_n
     L = a.layers or int(min(32, max(4, math.ceil(3 * L2_BYTES / est))))
-    d, f, k, layers = make_layers(a, L, device, rank, ws_n)
+    d, f, k, layers, pws = make_layers(a, L, device, rank, ws_n)
+    wtype = {"f16": spb.W_F16, "q8_0": spb.W_Q8_0, "q4_0": spb.W_Q4_0}[a.wtype]
+    w_bytes = {"f16": 2.0, "q8_0": 34 / 32, "q4_0": 18 / 32}[a.wtype]
+    pred_bytes = (d * PRED_RANK + PRED_RANK * f) * 2 if a.predictor else 0
     ws = spb.new_workspace(a.batch, d, f, 0, device)
     Us = [ly["U"] for ly in layers]
-    bytes_per_step = float(np.mean([active_bytes(d, U, a.batch) for U in Us]))
+    bytes_per_step = float(np.mean([active_bytes(d, U, a.batch, w_bytes, pred_bytes) for U in Us]))
 
     sharded = a.shard and ws_n > 1
 
     def fwd(ly, x=None, out=None):
         o = ly["out"] if out is None else out
-        spb.ffn_forward(*ly["W"], ly["x"] if x is None else x, ly["lab"], out=o,
+        xx = ly["x"] if x is None else x
+        if a.predictor:  # labels of this step from the layer's predictor
+            spb.predict(ly["P"][0], ly["P"][1], xx, k=k, out=ly["lab"], workspace=pws)
+        spb.ffn_forward(*ly["W"], xx, ly["lab"], wtype=wtype, out=o,
                         per_token_mask=bool(a.per_token), path=path, workspace=ws)
         if sharded:  # one all-reduce of the [B][d] partial outputs (NCCL)
             torch.distributed.all_reduce(o)
@@ -261,9 +323,12 @@ def run_ours(a):
     def e2e_body(ly):
         i = ly["i"]
         xin[i].copy_(pinned[i]["x"], non_blocking=True)
-        labin[i].copy_(pinned[i]["lab"], non_blocking=True)
-        spb.ffn_forward(*ly["W"], xin[i], labin[i], out=ly["out"], per_token_mask=bool(a.per_token), path=path,
-                        workspace=ws)
+        if a.predictor:  # labels are produced on the device from x
+            spb.predict(ly["P"][0], ly["P"][1], xin[i], k=k, out=labin[i], workspace=pws)
+        else:
+            labin[i].copy_(pinned[i]["lab"], non_blocking=True)
+        spb.ffn_forward(*ly["W"], xin[i], labin[i], wtype=wtype, out=ly["out"], per_token_mask=bool(a.per_token),
+                        path=path, workspace=ws)
         if sharded:
             torch.distributed.all_reduce(ly["out"])
         pinned[i]["out"].copy_(ly["out"], non_blocking=True)
@@ -281,16 +346,22 @@ def run_ours(a):
     peak, peak_kind = hbm_peak()
     t_step = ms / K / 1e3
     achieved = bytes_per_step / t_step / 1e9
-    launches_per_step = spb.lib().spb_ffn_launches(a.batch, path)
+    launches_per_step = spb.lib().spb_ffn_launches(a.batch, path) if a.wtype == "f16" else (
+        1 if a.batch <= 4 else 3)  # quantised weights: streaming kernel, or union + two GEMV launches
+    if a.predictor:
+        launches_per_step += 3  # predictor: hidden layer, logits, top-k selection
     rec = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": ws_n, "steps": K, "warmup": a.warmup,
         "ms_per_step": ms / K, "higher_is_better": True, "scaling": "strong" if sharded else "weak",
-        "vs_baseline": None, "dtype": "f16",
+        "vs_baseline": None, "dtype": a.wtype,
         "data": "synthetic (seeded N(0,0.02^2) fp16 weights, N(0,1) x, Zipf(0.8) activity; no dataset)",
         "config": {"workload": workload_name(a, int(np.mean([ly["U_full"] for ly in layers]))), "d": d,
                    "f_per_gpu": f, "batch": a.batch,
                    "k_per_token": k, "union_mean": float(np.mean(Us)), "layers_rotated": L,
-                   "per_token_mask": bool(a.per_token), "path": a.path,
+                   "per_token_mask": bool(a.per_token), "path": a.path, "weights": a.wtype,
+                   "predictor": (f"DejaVu rank {PRED_RANK}, top-{k} per token, run ahead of every layer "
+                                 f"({pred_bytes / 1e6:.1f} MB per layer counted in bytes_per_step)"
+                                 if a.predictor else None),
                    "l2": f"inputs larger than L2: {L} layer copies rotated, "
                          f"{L * bytes_per_step / 1e6:.0f} MB touched per cycle vs 126 MB L2",
                    "parallelism": (f"neuron-sharded tp{ws_n} + NCCL all-reduce" if sharded else
@@ -300,7 +371,8 @@ def run_ours(a):
                      "peak_source": f"{peak_kind} hbm_gbs", "traffic": traffic_from_profiles(a),
                      "bytes_per_step": bytes_per_step},
         "e2e": {"value": tokens / (ms_e2e / 1e3), "unit": "tokens/s",
-                "h2d_bytes_per_step": a.batch * d * 4 + a.batch * f * 4, "d2h_bytes_per_step": a.batch * d * 4,
+                "h2d_bytes_per_step": a.batch * d * 4 + (0 if a.predictor else a.batch * f * 4),
+                "d2h_bytes_per_step": a.batch * d * 4,
                 "ms_per_step": ms_e2e / K},
         "clocks": clocks,
         "gpu_launches": launches_per_step * K,
@@ -327,7 +399,13 @@ def traffic_from_profiles(a):
 def cpu_baseline(a, ly, budget=15.0):
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     from cpu_ffn import MaskedDenseFFN, time_steps
-    W = [w.float().cpu().numpy() for w in ly["W"]]
+    if a.wtype == "f16":
+        W = [w.float().cpu().numpy() for w in ly["W"]]
+    else:  # the CPU baseline computes with the dequantised weights (oracle dequantisation)
+        import oracle
+        qt = 8 if a.wtype == "q8_0" else 4
+        d = ly["x_np"].shape[1]
+        W = [oracle.dequantize(w.cpu().numpy(), qt, d) for w in ly["W"]]
     ffn = MaskedDenseFFN(*W)
     n, s = time_steps(ffn, ly["x_np"], ly["lab_np"], budget_s=budget)
     return {"value": a.batch * n / s, "unit": "tokens/s", "cores": ffn.threads, "kind": "port",

@@ -145,22 +145,31 @@ def quantize(w, wtype: int):
     return out
 
 
-def predict(p1, p2, x, k: int = 0, threshold: float = 0.0, *, return_idx: bool = False, stream=None):
+def predict_workspace(B: int, D: int, f: int, device=None):
+    """Scratch for spb_predict (allocate once, reuse: predict() then allocates nothing)."""
+    import torch
+    return torch.empty(int(lib().spb_predict_workspace_bytes(B, D, f)), dtype=torch.uint8, device=device or "cuda")
+
+
+def predict(p1, p2, x, k: int = 0, threshold: float = 0.0, *, return_idx: bool = False, out=None, workspace=None,
+            stream=None):
     """DejaVu predictor on the GPU (spb_predict): labels [B][f] (1 active).
 
     p1 [D][d] fp16, p2 [f][D] fp16, x [B][d] fp32.  k > 0 selects the top-k
     logits per token; k = 0 thresholds the logits.  With return_idx, also the
-    ascending active ids [B][k or f] and the per-token counts.
+    ascending active ids [B][k or f] and the per-token counts.  `out` ([B][f]
+    fp32) and `workspace` (predict_workspace) make the call allocation-free,
+    so it can be captured in a CUDA graph.
     """
     import torch
-    _require_cuda(p1, p2, x)
+    _require_cuda(p1, p2, x, out, workspace)
     B, d = x.shape
     D, f = p1.shape[0], p2.shape[0]
     dev = x.device
-    labels = torch.empty((B, f), dtype=torch.float32, device=dev)
+    labels = out if out is not None else torch.empty((B, f), dtype=torch.float32, device=dev)
     idx = torch.full((B, k if k > 0 else f), -1, dtype=torch.int32, device=dev) if return_idx else None
     counts = torch.zeros(B, dtype=torch.int32, device=dev) if return_idx else None
-    ws = torch.empty(int(lib().spb_predict_workspace_bytes(B, D, f)), dtype=torch.uint8, device=dev)
+    ws = workspace if workspace is not None else predict_workspace(B, D, f, dev)
     _check(lib().spb_predict(p1.data_ptr(), p2.data_ptr(), x.data_ptr(), B, d, D, f, k, threshold,
                              labels.data_ptr(), _ptr(idx), _ptr(counts), None, ws.data_ptr(), ws.numel(),
                              _stream(stream)), "spb_predict")

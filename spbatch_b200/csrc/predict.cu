@@ -20,6 +20,8 @@
 #include "spb_internal.h"
 #include "spb_scan.cuh"
 
+#include <algorithm>
+
 namespace spb {
 
 constexpr int kPredThreads = 256;
@@ -32,24 +34,36 @@ template <int NT>
 __device__ __forceinline__ void fixed_dot(const __half *__restrict__ row, const float *__restrict__ vs, int n,
                                           int nt, float (&acc)[NT]) {
     const int lane = threadIdx.x & 31;
+    constexpr int kBatch = 8;  // 16-byte loads in flight per lane (the FMA order is unchanged)
 #pragma unroll
     for (int t = 0; t < NT; ++t) acc[t] = 0.0f;
-    for (int c = lane; c < n / 8; c += 32) {
-        const uint4 wv = ld_stream_v4(row + (int64_t)c * 8);
-        const uint32_t *pw = reinterpret_cast<const uint32_t *>(&wv);
-        float w[8];
+    const int nch = n / 8;
+    for (int c0 = lane; c0 < nch; c0 += 32 * kBatch) {
+        uint4 wv[kBatch];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            const float2 f2 = h2f2(pw[q]);
-            w[2 * q] = f2.x;
-            w[2 * q + 1] = f2.y;
+        for (int u = 0; u < kBatch; ++u) {
+            const int c = c0 + u * 32;
+            wv[u] = c < nch ? ld_stream_v4(row + (int64_t)c * 8) : make_uint4(0u, 0u, 0u, 0u);
         }
 #pragma unroll
-        for (int t = 0; t < NT; ++t) {
-            if (t < nt) {
-                const float *v = vs + (int64_t)t * n + c * 8;
+        for (int u = 0; u < kBatch; ++u) {
+            const int c = c0 + u * 32;
+            if (c >= nch) break;
+            const uint32_t *pw = reinterpret_cast<const uint32_t *>(&wv[u]);
+            float w[8];
 #pragma unroll
-                for (int e = 0; e < 8; ++e) acc[t] = fmaf(w[e], v[e], acc[t]);
+            for (int q = 0; q < 4; ++q) {
+                const float2 f2 = h2f2(pw[q]);
+                w[2 * q] = f2.x;
+                w[2 * q + 1] = f2.y;
+            }
+#pragma unroll
+            for (int t = 0; t < NT; ++t) {
+                if (t < nt) {
+                    const float *v = vs + (int64_t)t * n + c * 8;
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) acc[t] = fmaf(w[e], v[e], acc[t]);
+                }
             }
         }
     }
@@ -66,8 +80,26 @@ pred_hidden_kernel(const __half *__restrict__ p1, const float *__restrict__ x, _
                    int d, int D, int rows_per_cta) {
     extern __shared__ __align__(16) float xs[];  // [kPredTokens][d]
     const int t0 = blockIdx.y * kPredTokens, nt = min(kPredTokens, B - t0);
-    for (int i = threadIdx.x; i < nt * d; i += blockDim.x)
-        xs[i] = __half2float(__float2half_rn(x[(int64_t)t0 * d + i]));
+    {  // float4 loads, several in flight per thread (d % 256 == 0)
+        const float4 *src = reinterpret_cast<const float4 *>(x + (int64_t)t0 * d);
+        const int n4 = nt * d / 4;
+        for (int base = threadIdx.x; base < n4; base += 4 * blockDim.x) {
+            float4 v[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int i = base + u * blockDim.x;
+                v[u] = i < n4 ? __ldg(src + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int i = base + u * blockDim.x;
+                if (i < n4)
+                    reinterpret_cast<float4 *>(xs)[i] =
+                        make_float4(__half2float(__float2half_rn(v[u].x)), __half2float(__float2half_rn(v[u].y)),
+                                    __half2float(__float2half_rn(v[u].z)), __half2float(__float2half_rn(v[u].w)));
+            }
+        }
+    }
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int r1 = min(D, (int)(blockIdx.x + 1) * rows_per_cta);
@@ -85,7 +117,20 @@ pred_logit_kernel(const __half *__restrict__ p2, const __half *__restrict__ hidd
                   int D, int f, int rows_per_cta) {
     extern __shared__ __align__(16) float hs[];  // [kPredTokens][D]
     const int t0 = blockIdx.y * kPredTokens, nt = min(kPredTokens, B - t0);
-    for (int i = threadIdx.x; i < nt * D; i += blockDim.x) hs[i] = __half2float(hidden[(int64_t)t0 * D + i]);
+    {  // 8 fp16 values per 16-byte load (D % 256 == 0)
+        const uint4 *src = reinterpret_cast<const uint4 *>(hidden + (int64_t)t0 * D);
+        const int n8 = nt * D / 8;
+        for (int i = threadIdx.x; i < n8; i += blockDim.x) {
+            const uint4 v = __ldg(src + i);
+            const uint32_t *pv = reinterpret_cast<const uint32_t *>(&v);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const float2 f2 = h2f2(pv[q]);
+                hs[i * 8 + 2 * q] = f2.x;
+                hs[i * 8 + 2 * q + 1] = f2.y;
+            }
+        }
+    }
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int j1 = min(f, (int)(blockIdx.x + 1) * rows_per_cta);
@@ -104,101 +149,164 @@ __device__ __forceinline__ uint32_t order_key(float v) {
 }
 
 constexpr int kSelThreads = 1024;
+constexpr int kSelWarps = kSelThreads / 32;
+
+// Exclusive block scan of one int per thread (kSelThreads threads); *total
+// receives the block sum.  Two __syncthreads.
+__device__ __forceinline__ int sel_block_scan(int v, int *warp_tot, int *total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int incl = warp_incl_scan(v);
+    if (lane == 31) warp_tot[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+        const int w = lane < kSelWarps ? warp_tot[lane] : 0;
+        const int wi = warp_incl_scan(w);
+        warp_tot[lane] = wi - w;
+        if (lane == 31) warp_tot[32] = wi;
+    }
+    __syncthreads();
+    *total = warp_tot[32];
+    return warp_tot[warp] + incl - v;
+}
 
 // One CTA per token.  k > 0: exact top-k (ties broken toward lower ids);
 // k == 0: logit >= threshold.  Writes labels [B][f] (1.0 / 0.0), the ascending
 // active list idx[t][0..count) (capacity `cap` per token) and counts[t].
+// The threshold key is found by an 8-bit radix select (4 passes, bins
+// searched by one warp with a suffix scan); then each thread owns a
+// contiguous run of indices, so two block scans place the equal keys (lowest
+// ids first) and the active ids in index order.
 __global__ void __launch_bounds__(kSelThreads)
 pred_select_kernel(const float *__restrict__ logits, int f, int k, float threshold, float *__restrict__ labels,
                    int32_t *__restrict__ idx, int cap, int32_t *__restrict__ counts) {
-    extern __shared__ uint32_t keys[];  // [f]
+    extern __shared__ uint32_t keys[];  // [f], then [kSelWarps][256] per-warp histograms
+    uint32_t *whist = keys + ((f + 3) & ~3);
     __shared__ uint32_t hist[256];
     __shared__ uint32_t sel_prefix, sel_mask;
     __shared__ int need;
     __shared__ int warp_tot[33];
     const int t = blockIdx.x;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const float *lg = logits + (int64_t)t * f;
-    for (int j = threadIdx.x; j < f; j += blockDim.x) keys[j] = order_key(lg[j]);
-    uint32_t thr_key = 0;
-    int take_eq = 0;  // how many keys equal to thr_key are active (lowest ids first)
-    if (k > 0 && k < f) {
-        if (threadIdx.x == 0) {
-            sel_prefix = 0u;
-            sel_mask = 0u;
-            need = k;
-        }
-        __syncthreads();
-        for (int shift = 24; shift >= 0; shift -= 8) {
-            for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0u;
-            __syncthreads();
-            const uint32_t pfx = sel_prefix, msk = sel_mask;
-            for (int j = threadIdx.x; j < f; j += blockDim.x) {
-                const uint32_t key = keys[j];
-                if ((key & msk) == pfx) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+    if ((f & 3) == 0) {  // float4 loads, four in flight per thread
+        const float4 *src = reinterpret_cast<const float4 *>(lg);
+        const int n4 = f >> 2;
+        for (int base = threadIdx.x; base < n4; base += 4 * blockDim.x) {
+            float4 v[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int i = base + u * blockDim.x;
+                v[u] = i < n4 ? __ldg(src + i) : make_float4(0.f, 0.f, 0.f, 0.f);
             }
-            __syncthreads();
-            if (threadIdx.x == 0) {
-                int rem = need;
-                int b = 255;
-                for (; b > 0; --b) {
-                    if ((int)hist[b] >= rem) break;
-                    rem -= (int)hist[b];
-                }
-                sel_prefix = pfx | ((uint32_t)b << shift);
-                sel_mask = msk | (255u << shift);
-                need = rem;
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int i = base + u * blockDim.x;
+                if (i < n4)
+                    reinterpret_cast<uint4 *>(keys)[i] =
+                        make_uint4(order_key(v[u].x), order_key(v[u].y), order_key(v[u].z), order_key(v[u].w));
             }
-            __syncthreads();
         }
-        thr_key = sel_prefix;
-        take_eq = need;
+    } else {
+        for (int j = threadIdx.x; j < f; j += blockDim.x) keys[j] = order_key(lg[j]);
+    }
+    const bool topk = k > 0 && k < f;
+    if (threadIdx.x == 0) {
+        sel_prefix = 0u;
+        sel_mask = 0u;
+        need = k;
     }
     __syncthreads();
-    // active flags in index order, then an ordered scan for the list positions
-    int carry = 0, eq_seen = 0;
-    for (int base = 0; base < f; base += blockDim.x) {
-        const int j = base + threadIdx.x;
-        const uint32_t key = j < f ? keys[j] : 0u;
-        int is_eq = (k > 0 && k < f && j < f && key == thr_key) ? 1 : 0;
-        // rank of this key among equal keys (by index) = eq_seen + exclusive scan
-        int eq_incl = warp_incl_scan(is_eq);
-        if ((threadIdx.x & 31) == 31) warp_tot[threadIdx.x >> 5] = eq_incl;
-        __syncthreads();
-        if (threadIdx.x < 32) {
-            const int v = threadIdx.x < (int)(blockDim.x >> 5) ? warp_tot[threadIdx.x] : 0;
-            const int vi = warp_incl_scan(v);
-            warp_tot[threadIdx.x] = vi - v;
-            if (threadIdx.x == 31) warp_tot[32] = vi;
+    if (topk) {
+        for (int shift = 24; shift >= 0; shift -= 8) {
+            // per-warp histograms: logits crowd into a few bins, so a shared
+            // histogram would serialise the whole block on those counters
+            for (int i = threadIdx.x; i < kSelWarps * 256; i += blockDim.x) whist[i] = 0u;
+            __syncthreads();
+            const uint32_t pfx = sel_prefix, msk = sel_mask;
+            uint32_t *wh = whist + warp * 256;
+            for (int j = threadIdx.x; j < f; j += blockDim.x) {
+                const uint32_t key = keys[j];
+                if ((key & msk) == pfx) atomicAdd(&wh[(key >> shift) & 255u], 1u);
+            }
+            __syncthreads();
+            if (threadIdx.x < 256) {
+                uint32_t sum = 0;
+                for (int w = 0; w < kSelWarps; ++w) sum += whist[w * 256 + threadIdx.x];
+                hist[threadIdx.x] = sum;
+            }
+            __syncthreads();
+            if (warp == 0) {
+                // lane l holds bins 255-8l .. 248-8l (descending); the answer is
+                // the highest bin b with (count of bins > b) < need <= (count of bins >= b)
+                uint32_t c[8], sum = 0;
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                    c[q] = hist[255 - 8 * lane - q];
+                    sum += c[q];
+                }
+                uint32_t incl = sum;  // inclusive scan over lanes (descending bins)
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const uint32_t n = __shfl_up_sync(0xffffffffu, incl, o);
+                    if (lane >= o) incl += n;
+                }
+                const int rem = need;
+                uint32_t before = incl - sum;  // keys in higher bins than this lane's
+                int found = -1, rem_out = 0;
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                    if (found < 0 && (int)(before + c[q]) >= rem) {
+                        found = 255 - 8 * lane - q;
+                        rem_out = rem - (int)before;
+                    }
+                    before += c[q];
+                }
+                const uint32_t ball = __ballot_sync(0xffffffffu, found >= 0);
+                const int src = ball ? __ffs(ball) - 1 : 31;
+                const int b = __shfl_sync(0xffffffffu, found >= 0 ? found : 0, src);
+                const int r = __shfl_sync(0xffffffffu, rem_out, src);
+                if (lane == 0) {
+                    sel_prefix = pfx | ((uint32_t)b << shift);
+                    sel_mask = msk | (255u << shift);
+                    need = r;
+                }
+            }
+            __syncthreads();
         }
-        __syncthreads();
-        const int eq_rank = eq_seen + warp_tot[threadIdx.x >> 5] + eq_incl - is_eq;
-        const int eq_total = warp_tot[32];
-        __syncthreads();
-        bool active = false;
-        if (j < f) {
-            if (k >= f) active = true;
-            else if (k > 0) active = key > thr_key || (is_eq && eq_rank < take_eq);
-            else active = lg[j] >= threshold;  // float compare: -0.0 >= 0.0 holds
-            labels[(int64_t)t * f + j] = active ? 1.0f : 0.0f;
-        }
-        int a = active ? 1 : 0;
-        int a_incl = warp_incl_scan(a);
-        if ((threadIdx.x & 31) == 31) warp_tot[threadIdx.x >> 5] = a_incl;
-        __syncthreads();
-        if (threadIdx.x < 32) {
-            const int v = threadIdx.x < (int)(blockDim.x >> 5) ? warp_tot[threadIdx.x] : 0;
-            const int vi = warp_incl_scan(v);
-            warp_tot[threadIdx.x] = vi - v;
-            if (threadIdx.x == 31) warp_tot[32] = vi;
-        }
-        __syncthreads();
-        const int pos = carry + warp_tot[threadIdx.x >> 5] + a_incl - a;
-        if (active && idx && pos < cap) idx[(int64_t)t * cap + pos] = j;
-        carry += warp_tot[32];
-        eq_seen += eq_total;
-        __syncthreads();
     }
-    if (threadIdx.x == 0 && counts) counts[t] = carry;
+    const uint32_t thr_key = sel_prefix;
+    const int take_eq = need;  // how many keys equal to thr_key are active (lowest ids first)
+    // contiguous index run of this thread
+    const int per = (f + kSelThreads - 1) / kSelThreads;
+    const int j0 = min(f, (int)threadIdx.x * per), j1 = min(f, j0 + per);
+    int n_eq = 0;
+    if (topk)
+        for (int j = j0; j < j1; ++j) n_eq += keys[j] == thr_key;
+    int tot;
+    int eq_rank = sel_block_scan(n_eq, warp_tot, &tot);  // equal keys before this run
+    int n_act = 0;
+    for (int j = j0; j < j1; ++j) {
+        bool active;
+        if (k >= f) active = true;
+        else if (k > 0) active = keys[j] > thr_key || (keys[j] == thr_key && eq_rank++ < take_eq);
+        else active = lg[j] >= threshold;  // float compare: -0.0 >= 0.0 holds
+        n_act += active;
+    }
+    __syncthreads();
+    int pos = sel_block_scan(n_act, warp_tot, &tot);
+    eq_rank -= n_eq;  // replay the same decisions, now writing
+    for (int j = j0; j < j1; ++j) {
+        bool active;
+        if (k >= f) active = true;
+        else if (k > 0) active = keys[j] > thr_key || (keys[j] == thr_key && eq_rank++ < take_eq);
+        else active = lg[j] >= threshold;
+        labels[(int64_t)t * f + j] = active ? 1.0f : 0.0f;
+        if (active) {
+            if (idx && pos < cap) idx[(int64_t)t * cap + pos] = j;
+            ++pos;
+        }
+    }
+    if (threadIdx.x == 0 && counts) counts[t] = tot;
 }
 
 int launch_predict(const __half *p1, const __half *p2, const float *x, int B, int d, int D, int f, int k,
@@ -207,8 +315,10 @@ int launch_predict(const __half *p1, const __half *p2, const float *x, int B, in
     const int sms = num_sms();
     const int ty = (B + kPredTokens - 1) / kPredTokens;
     {
+        // one row per warp when that fills the GPU: every row's loads are in
+        // flight at once (each warp's 8 KB row is the fixed-order dot unit)
         const int ctas = max(1, (2 * sms + ty - 1) / ty);
-        const int rows = (D + ctas - 1) / ctas;
+        const int rows = std::min((D + ctas - 1) / ctas, kPredWarps);
         const size_t smem = sizeof(float) * kPredTokens * d;
         if (smem > 200 * 1024) return fail(SPB_ERR_UNSUPPORTED, "spb_predict: d too large");
         if (int rc = ensure_smem((const void *)pred_hidden_kernel, smem)) return rc;
@@ -226,7 +336,7 @@ int launch_predict(const __half *p1, const __half *p2, const float *x, int B, in
         SPB_LAUNCH_CHECK("pred_logit_kernel");
     }
     {
-        const size_t smem = sizeof(uint32_t) * f;
+        const size_t smem = sizeof(uint32_t) * (((f + 3) & ~3) + kSelWarps * 256);
         if (smem > 200 * 1024) return fail(SPB_ERR_UNSUPPORTED, "spb_predict: f too large");
         if (int rc = ensure_smem((const void *)pred_select_kernel, smem)) return rc;
         const int cap = k > 0 ? k : f;
