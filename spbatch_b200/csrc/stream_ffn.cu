@@ -1,22 +1,30 @@
 // Streaming single-launch FFN for small batches (B <= 4) on CUDA cores.
 //
-// One cooperative launch (one CTA per SM, all resident) does the whole layer
-// -- batch union, gathered gate/up, ReLU*up, gathered down -- replacing
-// get_idx_cuda + mm_up + relu_and_mul + convert_fp32_to_fp16 + mm_down
-// (cuda/kernel.cu:566-816, 522-529, 321-356).
+// One launch (one CTA per SM) does the whole layer -- batch union, gathered
+// gate/up, ReLU*up, gathered down -- replacing get_idx_cuda + mm_up +
+// relu_and_mul + convert_fp32_to_fp16 + mm_down (cuda/kernel.cu:566-816,
+// 522-529, 321-356).
 //
-// Phase 1: each CTA reads the label columns of its share of the 32-neuron
-// words (fp32, active if > 0), writes the per-token ballots and their union
-// to the workspace, and zeroes its slice of `out`.  One grid barrier.
-// Phase 2: every CTA rebuilds the ascending union id list from the union
-// words (block scan of their popcounts) and takes an equal contiguous share
-// of it, so no CTA holds more than one neuron above the average.  For each of
-// its neurons j, one producer thread copies the three weight rows -- W_gate[j],
-// W_up[j] and W_down[j], each contiguous because W_down is stored [f][d] --
-// into a ring of shared-memory stages with 1-D bulk copies (cp.async.bulk,
-// completion counted as transaction bytes on an mbarrier).  With up to 8
-// stages of 24 KB (d = 4096, fp16) in flight per SM the HBM pipe stays full
-// without register staging.
+// Union.  B = 1: every CTA reads the whole label row (f fp32, active if > 0)
+// through L2 and builds the union words in shared memory itself, so no
+// grid-wide step is needed.  B >= 2: reading all B rows in every CTA costs
+// B x f x 4 bytes of hot-line L2 traffic per SM, so each CTA scans its share
+// of the 32-neuron words, publishes the ballots to the workspace, and after a
+// grid barrier (the launch is then cooperative) reads all words back.  CTA 0
+// zeroes `out` and publishes the launch number (taken from per-CTA tickets of
+// a monotonic counter); the other CTAs check it only before their final
+// reductions.
+//
+// Rows.  Every CTA rebuilds the ascending union list from the words (one
+// block scan) and takes an equal contiguous share of it, so no CTA holds more
+// than one neuron above the average.  For each of its neurons j one producer
+// thread copies the three weight rows -- W_gate[j], W_up[j] and W_down[j],
+// each contiguous because W_down is stored [f][d] -- into a ring of
+// shared-memory stages with 1-D bulk copies (cp.async.bulk, completion
+// counted as transaction bytes on an mbarrier).  With up to 8 stages of 24 KB
+// (d = 4096, fp16) in flight per SM the HBM pipe stays full without register
+// staging.  Launched with programmatic dependent launch (the prologue
+// overlaps the previous kernel's tail).
 //
 // The 16 consumer warps split the hidden dimension: thread `tid` owns the
 // 8-element chunks tid, tid + 512, ... of every row and keeps the
