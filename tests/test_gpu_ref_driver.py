@@ -42,11 +42,21 @@ def test_reference_driver_links_and_matches(tmp_path):
     print(f"spmm_test BS up projection (B=64, f=11008, d=4096): ours {ours:.4f} ms, reference {theirs:.4f} ms")
 
 
+def _driver_error(text):
+    """(largest |BS - naive|, largest |naive|) over the driver's mismatch lines."""
+    err = scale = 0.0
+    for a, b in re.findall(r"mismatch at \(\d+, \d+\): (\S+) vs (\S+)", text):
+        a, b = float(a), float(b)
+        err, scale = max(err, abs(a - b)), max(scale, abs(b))
+    return err, scale
+
+
 def _ffn_driver(binary, tmp_path, M=32, layer=0, iters=5):
     """ffn_test reads ../DejaVu_predictor/predictor_data/prosparse-llama-2-7b/
     mlp_label_<layer>.mmap (fp16 [8 + M][11008], first 8 rows skipped,
     cuda/utility.cu:7-26); the ProSparse dumps are not available, so a seeded
-    Zipf(0.8) dump with 10% activity per token stands in."""
+    Zipf(0.8) dump with 10% activity per token stands in (rows 0-7 are the
+    skipped header rows of read_idx, so token groups align with the dump)."""
     import numpy as np
     from spbatch_b200.workload import zipf_active_labels
     exe = os.path.join(REF, binary)
@@ -56,7 +66,13 @@ def _ffn_driver(binary, tmp_path, M=32, layer=0, iters=5):
     dump = tmp_path / "DejaVu_predictor" / "predictor_data" / "prosparse-llama-2-7b"
     run.mkdir(exist_ok=True)
     dump.mkdir(parents=True, exist_ok=True)
-    lab = zipf_active_labels(8 + M, 11008, 1101, seed=0, layer=layer).astype(np.float16)
+    # every group of 8 tokens (SPARSITY_GROUP_SIZE) shares one set: then the
+    # group-union semantics of MLP_BS and the per-token masking of the
+    # driver's MLP_naive define the same FFN (with independent synthetic
+    # sets they differ wherever ReLU(gate) of a neuron outside a token's own
+    # set is non-zero -- real ProSparse labels avoid that by construction)
+    grp = zipf_active_labels((8 + M) // 8, 11008, 1101, seed=0, layer=layer)
+    lab = np.repeat(grp, 8, axis=0).astype(np.float16)
     lab.tofile(dump / f"mlp_label_{layer}.mmap")
     p = subprocess.run([exe, str(tmp_path / f"{binary}.csv"), str(M), str(layer), str(iters)], cwd=run,
                        capture_output=True, text=True, timeout=300)
@@ -69,18 +85,20 @@ def test_reference_ffn_driver_links_and_matches(tmp_path):
     p = _ffn_driver("ffn_test_b200", tmp_path)
     assert p.returncode == 0, p.stderr[-2000:]
     # The driver prints every element that differs by more than 1.0 in
-    # absolute terms (cuda/utility.cu:151-166); with its randFill weights the
-    # outputs reach ~1e5, and MLP_naive rounds neither x nor h to fp16 while
-    # MLP_BS does (cuda/kernel.cu:978,1019), so bound the relative error.
-    worst = 0.0
-    for a, b in re.findall(r"mismatch at \(\d+, \d+\): (\S+) vs (\S+)", p.stdout):
-        a, b = float(a), float(b)
-        worst = max(worst, abs(a - b) / max(abs(b), 1.0))
-    assert worst <= 1e-2, f"relative error {worst:g} against the driver's MLP_naive"
+    # absolute terms (cuda/utility.cu:151-166).  Its randFill weights are
+    # U(-1, 1), so outputs are sums of ~1e3-1e4-sized terms of random sign;
+    # MLP_BS rounds x and h to fp16 (cuda/kernel.cu:978,1019) and MLP_naive
+    # does not, which moves an output by ~1e-4 of the term scale -- relative
+    # to an output that cancels to near zero that is large.  So the bound is
+    # relative to the largest output magnitude the driver reports.
+    err, scale = _driver_error(p.stdout)
+    assert err <= 1e-2 * max(scale, 1.0), f"max abs error {err:g} vs output scale {scale:g}"
     ours = _best(r"gate time: ([0-9.]+) ms", p.stdout)
     ref = _ffn_driver("ffn_test_ref", tmp_path)
     theirs = _best(r"gate time: ([0-9.]+) ms", ref.stdout) if ref.returncode == 0 else float("nan")
     pi = _best(r"PowerInfer time: ([0-9.]+) ms", p.stdout)
     cb = _best(r"cublas time: ([0-9.]+) ms", p.stdout)
-    print(f"ffn_test MLP_BS (B=32, 7B layer): ours {ours:.4f} ms, reference {theirs:.4f} ms; "
+    ref_err, ref_scale = _driver_error(ref.stdout)
+    print(f"ffn_test MLP_BS (B=32, 7B layer): ours {ours:.4f} ms (max error {err:g} at output scale {scale:g}), "
+          f"reference {theirs:.4f} ms (max error {ref_err:g} at scale {ref_scale:g}); "
           f"PowerInfer {pi:.4f} ms, cuBLAS dense {cb:.4f} ms")
