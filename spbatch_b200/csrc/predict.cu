@@ -31,7 +31,7 @@ constexpr int kPredTokens = 8;  // tokens per CTA (activations staged in shared 
 // Fixed-order dot of one fp16 row (n values, n % 256 == 0) with nt vectors
 // held in shared memory as fp32 (stride n); result broadcast to all lanes.
 template <int NT>
-__device__ __forceinline__ void fixed_dot(const __half *__restrict__ row, const float *__restrict__ vs, int n,
+__device__ __forceinline__ void fixed_dot(const __half *__restrict__ row, const __half *__restrict__ vs, int n,
                                           int nt, float (&acc)[NT]) {
     const int lane = threadIdx.x & 31;
     constexpr int kBatch = 8;  // 16-byte loads in flight per lane (the FMA order is unchanged)
@@ -60,9 +60,20 @@ __device__ __forceinline__ void fixed_dot(const __half *__restrict__ row, const 
 #pragma unroll
             for (int t = 0; t < NT; ++t) {
                 if (t < nt) {
-                    const float *v = vs + (int64_t)t * n + c * 8;
+                    // the staged vector holds fp16 values (exact: x and hidden
+                    // are fp16-rounded): one conflict-free 16-byte load per
+                    // chunk, converted exactly; same FMA order
+                    const uint4 hv = *reinterpret_cast<const uint4 *>(vs + (int64_t)t * n + c * 8);
+                    const uint32_t *ph = reinterpret_cast<const uint32_t *>(&hv);
+                    float ve[8];
 #pragma unroll
-                    for (int e = 0; e < 8; ++e) acc[t] = fmaf(w[e], v[e], acc[t]);
+                    for (int q = 0; q < 4; ++q) {
+                        const float2 f2 = h2f2(ph[q]);
+                        ve[2 * q] = f2.x;
+                        ve[2 * q + 1] = f2.y;
+                    }
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) acc[t] = fmaf(w[e], ve[e], acc[t]);
                 }
             }
         }
@@ -78,7 +89,7 @@ __device__ __forceinline__ void fixed_dot(const __half *__restrict__ row, const 
 __global__ void __launch_bounds__(kPredThreads)
 pred_hidden_kernel(const __half *__restrict__ p1, const float *__restrict__ x, __half *__restrict__ hidden, int B,
                    int d, int D, int rows_per_cta) {
-    extern __shared__ __align__(16) float xs[];  // [kPredTokens][d]
+    extern __shared__ __align__(16) __half xs[];  // [kPredTokens][d], fp16-rounded x
     const int t0 = blockIdx.y * kPredTokens, nt = min(kPredTokens, B - t0);
     {  // float4 loads, several in flight per thread (d % 256 == 0)
         const float4 *src = reinterpret_cast<const float4 *>(x + (int64_t)t0 * d);
@@ -93,10 +104,13 @@ pred_hidden_kernel(const __half *__restrict__ p1, const float *__restrict__ x, _
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
                 const int i = base + u * blockDim.x;
-                if (i < n4)
-                    reinterpret_cast<float4 *>(xs)[i] =
-                        make_float4(__half2float(__float2half_rn(v[u].x)), __half2float(__float2half_rn(v[u].y)),
-                                    __half2float(__float2half_rn(v[u].z)), __half2float(__float2half_rn(v[u].w)));
+                if (i < n4) {
+                    const __half2 h0 = __floats2half2_rn(v[u].x, v[u].y), h1 = __floats2half2_rn(v[u].z, v[u].w);
+                    uint2 pk;
+                    pk.x = *reinterpret_cast<const uint32_t *>(&h0);
+                    pk.y = *reinterpret_cast<const uint32_t *>(&h1);
+                    reinterpret_cast<uint2 *>(xs)[i] = pk;
+                }
             }
         }
     }
@@ -115,21 +129,12 @@ pred_hidden_kernel(const __half *__restrict__ p1, const float *__restrict__ x, _
 __global__ void __launch_bounds__(kPredThreads)
 pred_logit_kernel(const __half *__restrict__ p2, const __half *__restrict__ hidden, float *__restrict__ logits, int B,
                   int D, int f, int rows_per_cta) {
-    extern __shared__ __align__(16) float hs[];  // [kPredTokens][D]
+    extern __shared__ __align__(16) __half hs[];  // [kPredTokens][D]
     const int t0 = blockIdx.y * kPredTokens, nt = min(kPredTokens, B - t0);
     {  // 8 fp16 values per 16-byte load (D % 256 == 0)
         const uint4 *src = reinterpret_cast<const uint4 *>(hidden + (int64_t)t0 * D);
         const int n8 = nt * D / 8;
-        for (int i = threadIdx.x; i < n8; i += blockDim.x) {
-            const uint4 v = __ldg(src + i);
-            const uint32_t *pv = reinterpret_cast<const uint32_t *>(&v);
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                const float2 f2 = h2f2(pv[q]);
-                hs[i * 8 + 2 * q] = f2.x;
-                hs[i * 8 + 2 * q + 1] = f2.y;
-            }
-        }
+        for (int i = threadIdx.x; i < n8; i += blockDim.x) reinterpret_cast<uint4 *>(hs)[i] = __ldg(src + i);
     }
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -319,7 +324,7 @@ int launch_predict(const __half *p1, const __half *p2, const float *x, int B, in
         // flight at once (each warp's 8 KB row is the fixed-order dot unit)
         const int ctas = max(1, (2 * sms + ty - 1) / ty);
         const int rows = std::min((D + ctas - 1) / ctas, kPredWarps);
-        const size_t smem = sizeof(float) * kPredTokens * d;
+        const size_t smem = sizeof(__half) * kPredTokens * d;
         if (smem > 200 * 1024) return fail(SPB_ERR_UNSUPPORTED, "spb_predict: d too large");
         if (int rc = ensure_smem((const void *)pred_hidden_kernel, smem)) return rc;
         pred_hidden_kernel<<<dim3((D + rows - 1) / rows, ty), kPredThreads, smem, st>>>(p1, x, hidden, B, d, D, rows);
@@ -328,7 +333,7 @@ int launch_predict(const __half *p1, const __half *p2, const float *x, int B, in
     {
         const int ctas = max(1, (4 * sms + ty - 1) / ty);
         const int rows = (f + ctas - 1) / ctas;
-        const size_t smem = sizeof(float) * kPredTokens * D;
+        const size_t smem = sizeof(__half) * kPredTokens * D;
         if (smem > 200 * 1024) return fail(SPB_ERR_UNSUPPORTED, "spb_predict: D too large");
         if (int rc = ensure_smem((const void *)pred_logit_kernel, smem)) return rc;
         pred_logit_kernel<<<dim3((f + rows - 1) / rows, ty), kPredThreads, smem, st>>>(p2, hidden, logits, B, D, f,

@@ -22,7 +22,7 @@ def _stream():
     return torch.cuda.current_stream().cuda_stream
 
 
-def _mlp_bs(spb, library, cuda, W, x, lab, act="relu_and_mul_cuda"):
+def _mlp_bs(spb, library, cuda, W, x, lab, act="relu_and_mul_cuda", two_streams=False):
     """MLP_BS (cuda/ffn_test.cu:129-142) through the C++ API of `library`."""
     import torch
     wg, wu, wd = W
@@ -37,9 +37,10 @@ def _mlp_bs(spb, library, cuda, W, x, lab, act="relu_and_mul_cuda"):
     h = torch.zeros(B, f, device=cuda)
     out = torch.full((B, d), 7.0, device=cuda)
     s = _stream()
+    s1 = _stream() if two_streams else s  # MLP_BS passes a second stream for up (ffn_test.cu:139)
     F("get_idx_cuda")(lab.data_ptr(), merge.data_ptr(), act_n.data_ptr(), B, f, s)
     F("gate_and_up_mul_mat_cuda_sparse")(wg.data_ptr(), wu.data_ptr(), x.data_ptr(), gate.data_ptr(),
-                                         up.data_ptr(), merge.data_ptr(), f, B, d, act_n.data_ptr(), s, s)
+                                         up.data_ptr(), merge.data_ptr(), f, B, d, act_n.data_ptr(), s, s1)
     F(act)(gate.data_ptr(), up.data_ptr(), h.data_ptr(), B, f, s)
     F("down_mul_mat_cuda_sparse")(wd.data_ptr(), h.data_ptr(), out.data_ptr(), merge.data_ptr(), d, B, f,
                                   act_n.data_ptr(), s)
@@ -56,14 +57,15 @@ def _inputs(cuda, B, d, f, k, seed):
     return W, x, lab, [_dev(w, cuda) for w in W], _dev(x, cuda), _dev(lab, cuda)
 
 
-@pytest.mark.parametrize("act", ["relu_and_mul_cuda", "relu_relu_mul_cuda"])
-def test_mlp_bs_dropin_vs_oracle(spb, cuda, oracle_mod, act):
-    B, d, f = 16, 4096, 11008
+@pytest.mark.parametrize("act,B,two", [("relu_and_mul_cuda", 16, False), ("relu_relu_mul_cuda", 16, False),
+                                       ("relu_and_mul_cuda", 32, True), ("relu_and_mul_cuda", 64, False)])
+def test_mlp_bs_dropin_vs_oracle(spb, cuda, oracle_mod, act, B, two):
+    d, f = 4096, 11008
     W, x, lab, Wd, xd, labd = _inputs(cuda, B, d, f, 1101, 5)
-    r = _mlp_bs(spb, None, cuda, Wd, xd, labd, act)
+    r = _mlp_bs(spb, None, cuda, Wd, xd, labd, act, two_streams=two)
     merge, counts = oracle_mod.union(lab, 8)
     np.testing.assert_array_equal(r["act"], np.cumsum(counts))
-    for g in range(2):
+    for g in range(B // 8):
         np.testing.assert_array_equal(r["merge"][g, :counts[g]], merge[g, :counts[g]])
     g_ref = oracle_mod.up_compact(W[0], x, merge, counts, 8)
     u_ref = oracle_mod.up_compact(W[1], x, merge, counts, 8)

@@ -92,9 +92,11 @@ def test_reference_ffn_driver_links_and_matches(tmp_path):
     # to an output that cancels to near zero that is large.  So the bound is
     # relative to the largest output magnitude the driver reports.
     err, scale = _driver_error(p.stdout)
+    ref = _ffn_driver("ffn_test_ref", tmp_path)
+    print(f"ffn_test errors vs MLP_naive: ours {err:g} (scale {scale:g}), reference build "
+          f"{_driver_error(ref.stdout)}")
     assert err <= 1e-2 * max(scale, 1.0), f"max abs error {err:g} vs output scale {scale:g}"
     ours = _best(r"gate time: ([0-9.]+) ms", p.stdout)
-    ref = _ffn_driver("ffn_test_ref", tmp_path)
     theirs = _best(r"gate time: ([0-9.]+) ms", ref.stdout) if ref.returncode == 0 else float("nan")
     pi = _best(r"PowerInfer time: ([0-9.]+) ms", p.stdout)
     cb = _best(r"cublas time: ([0-9.]+) ms", p.stdout)
