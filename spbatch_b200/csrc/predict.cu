@@ -331,8 +331,11 @@ int launch_predict(const __half *p1, const __half *p2, const float *x, int B, in
         SPB_LAUNCH_CHECK("pred_hidden_kernel");
     }
     {
+        // at most four rows per warp: rows of D = 1024 are only 2 KB, so a
+        // warp walking many of them in turn is latency-bound; more CTAs keep
+        // more rows in flight (each CTA re-stages 8 x D fp16 from L2)
         const int ctas = max(1, (4 * sms + ty - 1) / ty);
-        const int rows = (f + ctas - 1) / ctas;
+        const int rows = std::min((f + ctas - 1) / ctas, 4 * kPredWarps);
         const size_t smem = sizeof(__half) * kPredTokens * D;
         if (smem > 200 * 1024) return fail(SPB_ERR_UNSUPPORTED, "spb_predict: D too large");
         if (int rc = ensure_smem((const void *)pred_logit_kernel, smem)) return rc;
