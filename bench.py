@@ -347,7 +347,7 @@ def run_ours(a):
     t_step = ms / K / 1e3
     achieved = bytes_per_step / t_step / 1e9
     launches_per_step = spb.lib().spb_ffn_launches(a.batch, path) if a.wtype == "f16" else (
-        1 if a.batch <= 4 else 3)  # quantised weights: streaming kernel, or union + two GEMV launches
+        -(-a.batch // 4))  # quantised weights: one streaming launch per group of up to 4 tokens
     if a.predictor:
         launches_per_step += 3  # predictor: hidden layer, logits, top-k selection
     rec = {

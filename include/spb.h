@@ -166,7 +166,7 @@ int spb_union_static(const float *idx, int B, int f, int group, int32_t *merge_i
 int spb_trace_enable(void *device_buffer, size_t slots);
 
 /* Kernel launches one spb_ffn_forward call makes for batch B and `path`
-   (fp16 weights, d <= 4096). */
+   (fp16 weights, d <= 4096, per-token mask, no index outputs). */
 int spb_ffn_launches(int B, int path);
 
 #ifdef __cplusplus

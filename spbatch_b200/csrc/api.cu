@@ -191,6 +191,38 @@ int spb_ffn_forward(const void *w_gate, const void *w_up, const void *w_down, in
         sa.zero_flag = ws.zero_flag;
         return launch_stream_ffn(sa, st);
     }
+    // With the per-token mask and no index outputs, token t's output depends
+    // only on its own active set, so a batch the streaming kernel cannot hold
+    // (quantised weights with B > 4, d > 4096 with B > 2) runs as consecutive
+    // streaming launches over token groups it can hold: each group reads
+    // its own union, at the streaming kernel's rate.
+    int chunk = 4;
+    while (chunk > 1 && !stream_ffn_supported(wtype, chunk, d)) chunk /= 2;
+    if (per_token_mask && !merge_idx_out && !count_out && stream_ffn_supported(wtype, chunk, d)) {
+        for (int t0 = 0; t0 < B; t0 += chunk) {
+            StreamFfnArgs sa{};
+            sa.wg = w_gate;
+            sa.wu = w_up;
+            sa.wd = w_down;
+            sa.wtype = wtype;
+            sa.x = x + (int64_t)t0 * d;
+            sa.idx = idx + (int64_t)t0 * f;
+            sa.B = B - t0 < chunk ? B - t0 : chunk;
+            sa.d = d;
+            sa.f = f;
+            sa.act = act;
+            sa.per_token = 1;
+            sa.out = out + (int64_t)t0 * d;
+            sa.err = ws.err;
+            sa.seg_bits = ws.seg_bits;
+            sa.tok_bits = ws.tok_bits;
+            sa.grid_bar = ws.grid_bar;
+            sa.launch_ctr = ws.launch_ctr;
+            sa.zero_flag = ws.zero_flag;
+            if (int rc = launch_stream_ffn(sa, st)) return rc;
+        }
+        return SPB_OK;
+    }
     PrepJobs jobs;
     jobs.zero_out = out;
     jobs.zero_n = (int64_t)B * d;
@@ -249,7 +281,7 @@ int spb_trace_enable(void *device_buffer, size_t slots) {
 int spb_ffn_launches(int B, int path) {
     if (path == SPB_PATH_AUTO) path = B <= kGemvMaxBatch ? SPB_PATH_GEMV : SPB_PATH_TENSOR;  // fp16 weights
     if (path == SPB_PATH_TENSOR) return 2;
-    return stream_ffn_supported(SPB_W_F16, B, 4096) ? 1 : 3;  // streaming kernel, or union + gate/up + down
+    return (B + 3) / 4;  // one streaming launch per group of up to 4 tokens (per-token mask)
 }
 
 }  // extern "C"

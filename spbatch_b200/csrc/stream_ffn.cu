@@ -289,7 +289,7 @@ __global__ void __launch_bounds__(kSfThreads, 1) stream_ffn_kernel(const SfArgs 
     if (a.local_union) {
         // One token: every CTA reads the whole label row (f fp32, active if
         // > 0) through L2 and builds the words itself -- no grid-wide step.
-        if ((a.f & 3) == 0) {
+        if ((a.f & 3) == 0 && (reinterpret_cast<uintptr_t>(a.idx) & 15u) == 0) {
             // float4 loads: lane l of a warp covers neurons 4(q0 + l) .. +3; eight
             // lanes' nibbles form one 32-neuron word.
             constexpr int UR = NT == 1 ? 8 : (NT == 2 ? 4 : 2);  // rows of 544 float4 in flight
