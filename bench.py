@@ -346,8 +346,7 @@ def run_ours(a):
     peak, peak_kind = hbm_peak()
     t_step = ms / K / 1e3
     achieved = bytes_per_step / t_step / 1e9
-    launches_per_step = spb.lib().spb_ffn_launches(a.batch, path) if a.wtype == "f16" else (
-        -(-a.batch // 4))  # quantised weights: one streaming launch per group of up to 4 tokens
+    launches_per_step = spb.lib().spb_ffn_launches(a.batch, d, wtype, path)
     if a.predictor:
         launches_per_step += 3  # predictor: hidden layer, logits, top-k selection
     rec = {

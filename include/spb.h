@@ -165,9 +165,9 @@ int spb_union_static(const float *idx, int B, int f, int group, int32_t *merge_i
  */
 int spb_trace_enable(void *device_buffer, size_t slots);
 
-/* Kernel launches one spb_ffn_forward call makes for batch B and `path`
-   (fp16 weights, d <= 4096, per-token mask, no index outputs). */
-int spb_ffn_launches(int B, int path);
+/* Kernel launches one spb_ffn_forward call makes for batch B, hidden size d,
+   weight format wtype and `path` (per-token mask, no index outputs). */
+int spb_ffn_launches(int B, int d, int wtype, int path);
 
 #ifdef __cplusplus
 }

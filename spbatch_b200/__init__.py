@@ -21,39 +21,59 @@ W_F16, W_Q8_0, W_Q4_0 = 0, 1, 2
 ACT_RELU_MUL, ACT_RELU_RELU_MUL = 0, 1
 PATH_AUTO, PATH_GEMV, PATH_TENSOR = 0, 1, 2
 
+DEBUG_LIB_PATH = os.path.join(PKG, "libspbatch_b200_debug.so")
+
 _lib = None
+_debug_lib = None
 
 
 class SpbError(RuntimeError):
     pass
 
 
+def _load(path: str) -> C.CDLL:
+    if not os.path.exists(path):
+        raise SpbError(f"{path} is missing: run `python -m spbatch_b200.build`")
+    L = C.CDLL(path)
+    _bind(L)
+    return L
+
+
 def lib() -> C.CDLL:
     """Loads libspbatch_b200.so (build it with ``python -m spbatch_b200.build``)."""
     global _lib
     if _lib is None:
-        if not os.path.exists(LIB_PATH):
-            raise SpbError(f"{LIB_PATH} is missing: run `python -m spbatch_b200.build`")
-        L = C.CDLL(LIB_PATH)
-        P, I, Z = C.c_void_p, C.c_int, C.c_size_t
-        L.spb_last_error.restype = C.c_char_p
-        L.spb_version.restype = I
-        L.spb_ffn_workspace_bytes.argtypes = [I, I, I, I]
-        L.spb_ffn_workspace_bytes.restype = Z
-        L.spb_union.argtypes = [P, I, I, I, P, P, P, P, Z, P]
-        L.spb_union_static.argtypes = [P, I, I, I, P, P, P, P]
-        L.spb_weight_row_bytes.argtypes = [I, I]
-        L.spb_weight_row_bytes.restype = C.c_int64
-        L.spb_quantize.argtypes = [P, I, I, I, P]
-        L.spb_dequantize_rows.argtypes = [P, I, I, I, P, P]
-        L.spb_predict_workspace_bytes.argtypes = [I, I, I]
-        L.spb_predict_workspace_bytes.restype = Z
-        L.spb_predict.argtypes = [P, P, P, I, I, I, I, I, C.c_float, P, P, P, P, P, Z, P]
-        L.spb_ffn_forward.argtypes = [P, P, P, I, P, P, I, I, I, I, I, I, P, P, P, P, Z, P]
-        L.spb_ffn_launches.argtypes = [I, I]
-        L.spb_trace_enable.argtypes = [P, Z]
-        _lib = L
+        _lib = _load(LIB_PATH)
     return _lib
+
+
+def debug_lib() -> C.CDLL:
+    """The test-hook build of the library (include/spb_debug.h); tests only."""
+    global _debug_lib
+    if _debug_lib is None:
+        _debug_lib = _load(DEBUG_LIB_PATH)
+        _debug_lib.spb_debug_config.argtypes = [C.c_int, C.c_longlong]
+    return _debug_lib
+
+
+def _bind(L: C.CDLL) -> None:
+    P, I, Z = C.c_void_p, C.c_int, C.c_size_t
+    L.spb_last_error.restype = C.c_char_p
+    L.spb_version.restype = I
+    L.spb_ffn_workspace_bytes.argtypes = [I, I, I, I]
+    L.spb_ffn_workspace_bytes.restype = Z
+    L.spb_union.argtypes = [P, I, I, I, P, P, P, P, Z, P]
+    L.spb_union_static.argtypes = [P, I, I, I, P, P, P, P]
+    L.spb_weight_row_bytes.argtypes = [I, I]
+    L.spb_weight_row_bytes.restype = C.c_int64
+    L.spb_quantize.argtypes = [P, I, I, I, P]
+    L.spb_dequantize_rows.argtypes = [P, I, I, I, P, P]
+    L.spb_predict_workspace_bytes.argtypes = [I, I, I]
+    L.spb_predict_workspace_bytes.restype = Z
+    L.spb_predict.argtypes = [P, P, P, I, I, I, I, I, C.c_float, P, P, P, P, P, Z, P]
+    L.spb_ffn_forward.argtypes = [P, P, P, I, P, P, I, I, I, I, I, I, P, P, P, P, Z, P]
+    L.spb_ffn_launches.argtypes = [I, I, I, I]
+    L.spb_trace_enable.argtypes = [P, Z]
 
 
 def _check(rc: int, what: str) -> None:
@@ -77,6 +97,18 @@ def _require_cuda(*ts):
             raise SpbError("spbatch_b200 operates on CUDA tensors only (no CPU fallback)")
         if t is not None and not t.is_contiguous():
             raise SpbError("spbatch_b200 needs contiguous tensors")
+
+
+def device_error(workspace) -> int:
+    """The workspace's sticky device error code (0: no bounded wait ran out).
+
+    Reads 4 bytes back to the host, so it synchronises with the stream."""
+    import numpy as np
+    return int(np.frombuffer(workspace[:4].cpu().numpy().tobytes(), np.uint32)[0])
+
+
+def clear_device_error(workspace) -> None:
+    workspace[:4].zero_()
 
 
 def workspace_bytes(B: int, d: int, f: int, group: int = 0) -> int:
@@ -111,11 +143,13 @@ def union(idx, group: int = 0, workspace=None, stream=None):
 
 def ffn_forward(w_gate, w_up, w_down, x, idx, *, wtype: int = W_F16, act: int = ACT_RELU_MUL,
                 per_token_mask: bool = True, path: int = PATH_AUTO, out=None, workspace=None,
-                merge_idx_out=None, count_out=None, stream=None):
+                merge_idx_out=None, count_out=None, stream=None, check: bool = False):
     """One sparse FFN layer on the GPU (see spb_ffn_forward in include/spb.h).
 
     w_gate / w_up / w_down: [f][d] rows (W_down stored transposed, as the
     reference stores it); x [B][d] fp32; idx [B][f] fp32 labels (> 0 active).
+    check=True waits for the layer and raises if a bounded device wait ran
+    out (the workspace's error word, which it then clears).
     """
     import torch
     _require_cuda(w_gate, w_up, w_down, x, idx, out, merge_idx_out, count_out)
@@ -128,6 +162,11 @@ def ffn_forward(w_gate, w_up, w_down, x, idx, *, wtype: int = W_F16, act: int = 
                                  idx.data_ptr(), B, d, f, act, int(per_token_mask), path, out.data_ptr(),
                                  _ptr(merge_idx_out), _ptr(count_out), ws.data_ptr(), ws.numel(),
                                  _stream(stream)), "spb_ffn_forward")
+    if check:
+        code = device_error(ws)
+        if code:
+            clear_device_error(ws)
+            raise SpbError(f"spb_ffn_forward: device wait ran out (code {code}); the output is not valid")
     return out
 
 

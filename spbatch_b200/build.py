@@ -22,6 +22,9 @@ ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 OBJ = os.path.join(PKG, "_build")
 LIB = os.path.join(PKG, "libspbatch_b200.so")
+# The same library with the test hooks of include/spb_debug.h (only api.cu
+# differs); loaded by the failure-path tests, never by the product path.
+DEBUG_LIB = os.path.join(PKG, "libspbatch_b200_debug.so")
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall",
@@ -44,10 +47,10 @@ def _deps_newer(src: str, obj: str) -> bool:
     return any(os.path.getmtime(d) > t for d in deps)
 
 
-def _compile(src: str, force: bool, verbose_ptxas: bool) -> str:
-    obj = os.path.join(OBJ, os.path.basename(src)[:-3] + ".o")
+def _compile(src: str, force: bool, verbose_ptxas: bool, debug: bool = False) -> str:
+    obj = os.path.join(OBJ, os.path.basename(src)[:-3] + ("_debug.o" if debug else ".o"))
     if force or _deps_newer(src, obj):
-        cmd = [nvcc(), *ARCH, *FLAGS, "-c", src, "-o", obj]
+        cmd = [nvcc(), *ARCH, *FLAGS, *(["-DSPB_DEBUG_HOOKS"] if debug else []), "-c", src, "-o", obj]
         if verbose_ptxas:
             cmd.insert(1, "-Xptxas=-v")
         subprocess.check_call(cmd)
@@ -59,8 +62,11 @@ def build(force: bool = False, verbose_ptxas: bool = False) -> str:
     srcs = sorted(glob.glob(os.path.join(CSRC, "*.cu")))
     with cf.ThreadPoolExecutor(max_workers=min(8, len(srcs))) as ex:
         objs = list(ex.map(lambda s: _compile(s, force, verbose_ptxas), srcs))
-    if force or not os.path.exists(LIB) or any(os.path.getmtime(o) > os.path.getmtime(LIB) for o in objs):
-        subprocess.check_call([nvcc(), *ARCH, "-shared", "-o", LIB, *objs, "-lcuda"])
+    dbg = _compile(os.path.join(CSRC, "api.cu"), force, False, debug=True)
+    dobjs = [dbg if os.path.basename(o) == "api.o" else o for o in objs]
+    for lib, ob in ((LIB, objs), (DEBUG_LIB, dobjs)):
+        if force or not os.path.exists(lib) or any(os.path.getmtime(o) > os.path.getmtime(lib) for o in ob):
+            subprocess.check_call([nvcc(), *ARCH, "-shared", "-o", lib, *ob, "-lcuda"])
     return LIB
 
 

@@ -5,6 +5,9 @@
 #include <vector>
 
 #include "spb_internal.h"
+#ifdef SPB_DEBUG_HOOKS
+#include "spb_debug.h"
+#endif
 
 namespace spb {
 
@@ -68,6 +71,10 @@ void *trace_buffer(size_t slots) {
     return g_trace_buf && slots <= g_trace_slots ? g_trace_buf : nullptr;
 }
 
+static DebugHooks g_debug;
+
+const DebugHooks &debug_hooks() { return g_debug; }
+
 static bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 }  // namespace spb
@@ -127,39 +134,31 @@ int spb_ffn_forward(const void *w_gate, const void *w_up, const void *w_down, in
     if (path == SPB_PATH_TENSOR) {
         if (wtype != SPB_W_F16) return fail(SPB_ERR_UNSUPPORTED, "spb_ffn_forward: tensor path serves fp16 weights");
         if (B > 256) return fail(SPB_ERR_UNSUPPORTED, "spb_ffn_forward: tensor path serves B <= 256");
-        if (d % 128 != 0) return fail(SPB_ERR_INVALID, "spb_ffn_forward: tensor path needs d % 128 == 0");
-        PrepJobs jobs;
-        jobs.zero_out = out;
-        jobs.zero_n = (int64_t)B * d;
-        jobs.zero_u32 = ws.tile_cnt;
-        jobs.zero_u32_n = 2 * (int64_t)ws.T;
-        jobs.x = x;
-        jobs.x16 = ws.x16;
-        jobs.B = B;
-        jobs.Np = ws.Np;
-        jobs.d = d;
-        int rc = launch_union_bits(idx, B, f, B, ws.tok_bits, ws.seg_bits, jobs, st);
-        if (rc) return rc;
+        if (d % 256 != 0) return fail(SPB_ERR_INVALID, "spb_ffn_forward: tensor path needs d % 256 == 0");
+        // one cooperative launch: union, fp16 activations and the zeroed
+        // output are its first phase
         TcLaunch L{};
         L.wg = w_gate;
         L.wu = w_up;
         L.wd = w_down;
+        L.labels = idx;
+        L.x = x;
+        L.gbar = ws.gbar;
         L.x16 = ws.x16;
         L.h16 = ws.h16;
+        L.ready = ws.ready;
+        L.fpad = ws.fpad;
         L.seg_bits = ws.seg_bits;
         L.tok_bits = ws.tok_bits;
         L.out = out;
         L.merge_out = merge;
         L.count_out = count;
-        L.partial = ws.partial;
-        L.tile_cnt = ws.tile_cnt;
-        L.tile_ready = ws.tile_ready;
+        L.xchg = ws.xchg;
         L.err = ws.err;
         L.B = B;
         L.Np = ws.Np;
         L.d = d;
         L.f = f;
-        L.fpad = ws.fpad;
         L.act = act;
         L.per_token = per_token_mask;
         L.grid = num_sms() < kMaxTcGrid ? num_sms() : kMaxTcGrid;
@@ -278,10 +277,29 @@ int spb_trace_enable(void *device_buffer, size_t slots) {
     return SPB_OK;
 }
 
-int spb_ffn_launches(int B, int path) {
-    if (path == SPB_PATH_AUTO) path = B <= kGemvMaxBatch ? SPB_PATH_GEMV : SPB_PATH_TENSOR;  // fp16 weights
-    if (path == SPB_PATH_TENSOR) return 2;
-    return (B + 3) / 4;  // one streaming launch per group of up to 4 tokens (per-token mask)
+#ifdef SPB_DEBUG_HOOKS
+int spb_debug_config(int key, long long value) {
+    switch (key) {
+        case SPB_DEBUG_TIMEOUT_NS: g_debug.timeout_ns = value > 0 ? (uint64_t)value : 0; return SPB_OK;
+        case SPB_DEBUG_INJECT: g_debug.inject = (int)value; return SPB_OK;
+        case SPB_DEBUG_TC_NKB: g_debug.nkb = (int)value; return SPB_OK;
+        case SPB_DEBUG_TC_STAGES: g_debug.stages = (int)value; return SPB_OK;
+        case SPB_DEBUG_TC_HINT_ACC: g_debug.hint_acc = (uint32_t)value; return SPB_OK;
+        case SPB_DEBUG_TC_HINT: g_debug.hint = (uint32_t)value; return SPB_OK;
+        default: return fail(SPB_ERR_INVALID, "spb_debug_config: unknown key");
+    }
+}
+#endif
+
+int spb_ffn_launches(int B, int d, int wtype, int path) {
+    if (B <= 0 || d <= 0) return 0;
+    if (path == SPB_PATH_AUTO) path = (B <= kGemvMaxBatch || wtype != SPB_W_F16) ? SPB_PATH_GEMV : SPB_PATH_TENSOR;
+    if (path == SPB_PATH_TENSOR) return 1;  // one cooperative tensor-core launch
+    if (stream_ffn_supported(wtype, B, d)) return 1;
+    int chunk = 4;  // the token-group split spb_ffn_forward makes
+    while (chunk > 1 && !stream_ffn_supported(wtype, chunk, d)) chunk /= 2;
+    if (stream_ffn_supported(wtype, chunk, d)) return (B + chunk - 1) / chunk;
+    return 3;  // union + fallback gate/up GEMV + down GEMV
 }
 
 }  // extern "C"

@@ -51,17 +51,17 @@ struct Workspace {
     unsigned long long *launch_ctr;  // [1] streaming kernel: monotonic CTA ticket counter
     unsigned long long *grid_bar;    // [1] streaming kernel: grid-barrier arrival counter
     unsigned long long *zero_flag;   // [1] streaming kernel: launch number + 1 once `out` is zeroed
-    uint32_t *tile_cnt;    // [T] per-tile split-K arrival counters (zeroed per launch)
-    uint32_t *tile_ready;  // [T] per-tile "h published" flags (zeroed per launch)
     uint32_t *tok_bits;    // [B][W] per-token activity bits
     uint32_t *seg_bits;    // [S][W] per-segment union bits
     int32_t *merge_idx;    // [S][f] compacted ascending neuron ids
     int32_t *counts;       // [S + 1] per-segment counts (+1 spare)
     __half *h;             // [f][B] fp16 intermediate of the CUDA-core path
     __half *x16;           // [Np][d] fp16 activations of the tensor path
-    __half *h16;           // [Np][fpad] fp16 h of the tensor path (K-major)
-    float *partial;        // [kMaxTcGrid][2][Np][128] split-K partial sums
-    int T, Np, fpad;
+    unsigned int *gbar;    // [2] tensor path: grid barrier (arrival count, generation)
+    uint32_t *ready;       // [kMaxTcGrid / 2] tensor path: per-cluster h-publication counters (zeroed per launch)
+    __half *h16;           // [Np][fpad] tensor path: fp16 h, K-major per token
+    float *xchg;           // [kMaxTcGrid][Np][64] tensor path: per-CTA gate/up exchange slots
+    int Np, fpad;
     size_t bytes;
 };
 
@@ -77,8 +77,6 @@ inline Workspace carve_workspace(void *base, int B, int d, int f, int group) {
     int S = group <= 0 ? 1 : (B + group - 1) / group;
     int W = words_of(f);
     Workspace w{};
-    w.T = (f + 127) / 128;
-    w.fpad = w.T * 128;
     w.Np = B <= 256 ? padded_batch(B) : 0;
     size_t off = 0;
     auto take = [&](size_t n) {
@@ -86,13 +84,14 @@ inline Workspace carve_workspace(void *base, int B, int d, int f, int group) {
         off += align256(n);
         return base ? (void *)((char *)base + o) : nullptr;
     };
-    uint32_t *sync = (uint32_t *)take(sizeof(uint32_t) * (64 + 2 * (size_t)w.T));
+    w.fpad = (f + 63) / 64 * 64;
+    uint32_t *sync = (uint32_t *)take(sizeof(uint32_t) * (64 + kMaxTcGrid / 2));
     w.err = sync;
     w.launch_ctr = sync ? reinterpret_cast<unsigned long long *>(sync + 16) : nullptr;
     w.zero_flag = sync ? reinterpret_cast<unsigned long long *>(sync + 24) : nullptr;
     w.grid_bar = sync ? reinterpret_cast<unsigned long long *>(sync + 32) : nullptr;
-    w.tile_cnt = sync ? sync + 64 : nullptr;
-    w.tile_ready = sync ? sync + 64 + w.T : nullptr;
+    w.ready = sync ? sync + 64 : nullptr;
+    w.gbar = sync ? sync + 40 : nullptr;
     w.tok_bits = (uint32_t *)take(sizeof(uint32_t) * (size_t)B * W);
     w.seg_bits = (uint32_t *)take(sizeof(uint32_t) * (size_t)S * W);
     w.merge_idx = (int32_t *)take(sizeof(int32_t) * (size_t)S * f);
@@ -101,7 +100,7 @@ inline Workspace carve_workspace(void *base, int B, int d, int f, int group) {
     if (d > 0 && w.Np > 0) {
         w.x16 = (__half *)take(sizeof(__half) * (size_t)w.Np * d);
         w.h16 = (__half *)take(sizeof(__half) * (size_t)w.Np * w.fpad);
-        w.partial = (float *)take(sizeof(float) * (size_t)kMaxTcGrid * 2 * w.Np * 128);
+        w.xchg = (float *)take(sizeof(float) * (size_t)kMaxTcGrid * w.Np * 64);
     }
     w.bytes = off;
     return w;

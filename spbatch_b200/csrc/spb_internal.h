@@ -75,19 +75,36 @@ int launch_dropin_up(const __half *wg, const __half *wu, const float *x, float *
 int launch_dropin_down(const __half *wd, const float *h, float *out, const int32_t *merge_idx,
                        const int32_t *act_cum, int B, int d, int f, int G, cudaStream_t st);
 
-// tc_ffn.cu -- tcgen05 tensor-core path (one persistent launch after the union)
+// tc_ffn.cu -- tcgen05 tensor-core path (one launch after the union)
 struct TcLaunch {
     const void *wg, *wu, *wd;
-    const __half *x16;
-    __half *h16;
-    const uint32_t *seg_bits, *tok_bits;
+    const float *labels;      // [B][f] fp32 labels, or null when tok_in is given
+    const uint32_t *tok_in;   // [B][W] per-token activity bits, or null
+    const float *x;           // [B][d]
+    __half *x16;              // [Np][d] workspace
+    __half *h16;              // [Np][fpad] workspace
+    uint32_t *seg_bits, *tok_bits;
     float *out;
     int32_t *merge_out, *count_out;
-    float *partial;
-    uint32_t *tile_cnt, *tile_ready, *err;
+    float *xchg;              // [grid][Np][64] partner-exchange slots
+    uint32_t *ready;          // [grid / 2] per-cluster counters
+    unsigned int *gbar;       // [2] grid barrier (count, generation), zero when first used
+    uint32_t *err;
     int B, Np, d, f, fpad, act, per_token, grid;
 };
 int launch_ffn_tc(const TcLaunch &L, cudaStream_t st);
+
+// Test hooks: settable only in libraries built with SPB_DEBUG_HOOKS (through
+// spb_debug_config); all zero in the product library.
+struct DebugHooks {
+    uint64_t timeout_ns = 0;  // bounded-wait limit of the tensor path (0: 2 s)
+    int inject = 0;           // 1: the tensor path's rank-1 CTAs never signal their results
+    int nkb = 0;              // tensor path: force K blocks per gate/up stage
+    int stages = 0;           // tensor path: cap the ring depth
+    uint32_t hint_acc = 0;    // tensor path: suspend hint of the epilogue's accumulator waits (ns)
+    uint32_t hint = 0;        // tensor path: suspend hint of the ring waits (ns)
+};
+const DebugHooks &debug_hooks();
 
 // predict.cu -- low-rank activity predictor
 int launch_predict(const __half *p1, const __half *p2, const float *x, int B, int d, int D, int f, int k,

@@ -1,48 +1,46 @@
-// Tensor-core sparse FFN layer (tcgen05 / TMEM), one persistent launch.
+// Tensor-core sparse FFN layer (tcgen05 / TMEM), one launch after the union.
 //
 // Replaces the reference's mm_up (x2) + relu_and_mul + mm_down sequence
 // (cuda/kernel.cu:595-816, 971-1048; mma.sync m16n8k16 with ldmatrix) for
-// batches whose union forms real MMA tiles.  Everything after the union
-// launch happens in ffn_tc_kernel, one CTA per SM:
+// batches whose union forms real MMA tiles.
 //
-//  gate/up units   a 128-neuron tile of the batch union (positions
-//                  [128 i, 128 i + 128) of the ascending index list) times a
-//                  K-slice of d.  Each ring stage holds one K group: the
-//                  gathered W_gate and W_up rows for nkb 64-wide K blocks (a
-//                  contiguous 128*nkb-byte run per row) plus one copy of the
-//                  matching fp16 activations, shared by both matrices.  The
-//                  gathered rows arrive by cp.async (a warp copies whole row
-//                  runs per instruction), the activations by 2D TMA tiles,
-//                  all in the 128-byte-swizzled K-major layout the MMA reads.
-//                  A stage's barrier completes on the producers' cp.async
-//                  arrivals plus the TMA transaction bytes, so no producer
-//                  waits on its own copies.  The copy rate of the four
-//                  producer warps follows the bytes in flight, so the stage
-//                  size is chosen to keep the most weight bytes in flight in
-//                  the ring (three or more stages).  Per stage one thread issues
-//                  tcgen05.mma.kind::f16 M=128 x N=Np x K=16 into two TMEM
-//                  accumulators.  When several CTAs split a tile's K range,
-//                  each writes its fp32 partials and the last to arrive
-//                  (atomic per-tile counter) reduces them in fixed order.  The
-//                  epilogue applies ReLU(gate)*up (or dReLU) and the per-token
-//                  mask, rounds h to fp16 (cuda/kernel.cu:1019) into a K-major
-//                  buffer and publishes a per-tile ready flag.
-//  down unit       a 256-column slice of the output times a chunk of the
-//                  union: W_down rows (stored [f][d], so each row contributes
-//                  a contiguous 512-byte run) are the MN-major A operand, h the
-//                  K-major B operand; out^T[2 x 128 x Np] accumulates in TMEM
-//                  and is added into the pre-zeroed output with fp32
-//                  reductions.  The W_down rows of a stage are copied as soon
-//                  as its ring slot is free -- they overlap the tail of the
-//                  gate/up phase -- and only the stage's h tile waits for the
-//                  ready flags of the gate/up tiles it reads.
+// The launch is cooperative (every CTA is resident, one per SM) and grouped
+// in clusters of two CTAs.  Each CTA runs two phases.
+//
+//   gate/up   Cluster c owns the contiguous union positions [U c / C,
+//             U (c+1) / C) (C clusters), so every cluster gathers the same
+//             number of rows to within one, and walks them in tiles of at
+//             most 128 neurons.  CTA rank 0 multiplies the tile's gathered
+//             W_gate rows with the batch, CTA rank 1 the W_up rows
+//             (tcgen05.mma.kind::f16, M = 128 rows, N = Np tokens, K = d,
+//             fp32 accumulator in TMEM).  Each ring stage holds nkb 64-wide K
+//             blocks of the rows (cp.async, a 128 * nkb-byte run per row)
+//             and the activation tile (TMA), both in the 128-byte-swizzled
+//             K-major layout the MMA reads.  The pair then trades halves: a
+//             CTA writes its results for the partner's 64 rows to its
+//             workspace slot and signals the partner's mbarrier (release at
+//             cluster scope); with the partner's half it forms h = act(gate,
+//             up) * mask for its own 64 rows, rounds it to fp16
+//             (cuda/kernel.cu:1019) and stores it K-major ([token][position])
+//             in the workspace.  A per-cluster counter published with release
+//             semantics tells the down phase which positions are ready.
+//   down      Unit (m, k): output columns [256 m, 256 m + 256) times union
+//             chunk k (64-aligned positions [Q_k, Q_k+1), about U / KC of
+//             them).  W_down rows (stored [f][d]: a contiguous 512-byte run
+//             per row) are the MN-major A operand, copied by cp.async as soon
+//             as a ring slot is free -- they overlap the end of the gate/up
+//             phase; the h tile (TMA) waits for the counters of the clusters
+//             that produced it.  out^T[256 x Np] accumulates over the whole
+//             chunk in TMEM and is added to the pre-zeroed output with 16-byte
+//             fp32 reductions, so every output element receives KC
+//             contributions.
 //
 // Warp roles (544 threads): warps 0-3 epilogue (TMEM lanes 0-127), warps 4-15
-// producers (cp.async + TMA), warp 16 TMEM allocator + MMA issuer.  Waiting
-// threads sleep on the mbarrier (try_wait with a suspend hint) instead of
-// spinning, which would steal shared-memory bandwidth from the producers.
-// Every wait is bounded (2 s of %globaltimer); on timeout the kernel records an
-// error code in the workspace and unwinds instead of hanging.
+// producers, warp 16 TMEM allocation and MMA issue.  Every wait is bounded
+// (2 s of %globaltimer); when one runs out the kernel records a code in the
+// workspace's error word, stops issuing work, waits for its own copies (the
+// cp.async groups and the TMA barriers) and its MMAs (the last commit) to
+// land, frees its TMEM and returns.
 #include "spb_internal.h"
 #include "spb_scan.cuh"
 #include "tc_ptx.cuh"
@@ -50,7 +48,6 @@
 #include <cuda.h>
 
 #include <algorithm>
-#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -60,59 +57,80 @@ namespace spb {
 
 using namespace ptx;
 
-// Warp roles: 0-3 epilogue, 4-15 producers, 16 MMA.  The cp.async rate of a
-// warp is bounded by the copies it can keep in flight, so the copy rate of
-// the CTA grows with the number of producer warps (4 warps: ~30 GB/s per SM
-// on a 512-byte row gather, 8 warps: ~50 GB/s in isolation).
+constexpr int kEpiWarps = 4;
+constexpr int kProducerWarp0 = kEpiWarps;
 constexpr int kProducerWarps = 12;
-constexpr int kProducerWarp0 = 4;
+constexpr int kProducerThreads = kProducerWarps * 32;
 constexpr int kMmaWarp = kProducerWarp0 + kProducerWarps;
-constexpr int kTcThreads = (kMmaWarp + 1) * 32;
-constexpr int kTileM = 128;          // neurons per gate/up tile, rows per MMA
-constexpr int kDnCols = 256;         // output columns per down item (two M=128 tiles)
+constexpr int kTmaWarp = kMmaWarp + 1;
+constexpr int kTcThreads = (kTmaWarp + 1) * 32;
+constexpr int kTcWarps = kTcThreads / 32;
+constexpr int kTileM = 128;          // neurons per gate/up tile (MMA M)
+constexpr int kDnRows = 64;          // union positions per down stage
+constexpr int kSlice = 256;          // output columns per down unit (two M = 128 MMAs)
 constexpr uint32_t kATile = 16384;   // 128 rows x 128 bytes (one 64-wide K block)
-constexpr int kMaxStages = 8;
-constexpr int kMaxGuUnits = 4;       // gate/up units per CTA the shared id table holds
-constexpr uint64_t kTimeoutNs = 2000000000ull;
+constexpr uint32_t kDnLbo = (kDnRows / 8) * 1024;  // byte distance between 64-column blocks of a down stage
+constexpr uint32_t kDnWBytes = 4 * kDnLbo;         // 64 rows x 256 columns fp16
+constexpr int kMaxUnits = 8;          // ring units (a gate/up stage takes one or two, a down stage one)
+constexpr int kMaxBufs = 16;
+constexpr uint32_t kTmemCols = 512;
+constexpr int kEpiBar = 1;           // named barrier of the epilogue warps
+constexpr uint64_t kDefaultTimeoutNs = 2000000000ull;
 
-enum : uint32_t { kErrTimeoutFull = 1, kErrTimeoutEmpty = 2, kErrTimeoutAcc = 3, kErrTimeoutFlag = 4 };
-
-struct TcCtl {
-    uint64_t full[kMaxStages];
-    uint64_t empty[kMaxStages];
-    uint64_t acc_full;
-    uint64_t acc_empty;
-    uint32_t tmem_base;
-    volatile int abort;
-    int is_last;
-    int pad;
+enum : uint32_t {
+    kErrTimeoutFull = 1,   // MMA issuer: a stage's copies never landed
+    kErrTimeoutEmpty = 2,  // producer: a stage was never released by the MMAs
+    kErrTimeoutAcc = 3,    // accumulator hand-off between MMA issuer and epilogue
+    kErrTimeoutXchg = 4,   // the partner CTA's gate/up results never arrived
+    kErrTimeoutFlag = 5,   // down phase: a cluster never published its h
+    kErrTimeoutGrid = 6,   // the grid barrier after the union never completed
 };
 
-// How the layer is cut into units; every thread derives the same plan from U.
-struct Plan {
-    int U, T, Sk, ngu, KG, MT, KC, ndn;
+struct TcCtl {
+    // one of each per ring unit; every occupancy of a unit completes one
+    // phase of all three (units past a stage's first arm with no bytes)
+    uint64_t full[kMaxUnits];    // producers' cp.async arrivals
+    uint64_t tma[kMaxUnits];     // TMA bytes of the stage's activation / h tile
+    uint64_t empty[kMaxUnits];   // MMA commit: the unit may be overwritten
+    uint64_t acc_full[kMaxBufs];
+    uint64_t acc_empty[kMaxBufs];
+    uint64_t xchg_full;   // partner: its results for this CTA's rows are in its slot
+    uint64_t xchg_free;   // partner: it has read this CTA's slot
+    uint64_t ids_ready;   // epilogue: the down unit's ids are emitted
+    uint32_t tmem_base;
+    volatile int abort;
 };
 
 struct TcArgs {
     const __half *wg, *wu, *wd;  // [f][d]
-    __half *h16;                 // [Np][fpad]
-    const uint32_t *seg_bits;    // [W]
-    const uint32_t *tok_bits;    // [B][W]
+    const float *labels;         // [B][f] fp32 labels (> 0 active), or null with tok_in
+    const uint32_t *tok_in;      // [B][W] per-token activity bits given by the caller, or null
+    const float *x;              // [B][d] fp32 activations
+    __half *x16;                 // [Np][d] fp16 activations (rows >= B zero), written in phase 0
+    __half *h16;                 // [Np][fpad] h, K-major per token
+    uint32_t *seg_bits;          // [W] batch union, written in phase 0
+    uint32_t *tok_bits;          // [B][W] per-token bits, written in phase 0
+    unsigned int *gbar;          // [2] grid barrier: arrival count, generation
     float *out;                  // [B][d], zero on entry
     int32_t *merge_out;          // [f]
     int32_t *count_out;          // [1]
-    float *partial;              // [grid][2][Np][128]
-    uint32_t *tile_cnt;          // [Tmax], zero on entry
-    uint32_t *tile_ready;        // [Tmax], zero on entry
+    float *xchg;                 // [grid][Np][64] per-CTA exchange slots
+    uint32_t *ready;             // [grid / 2] per-cluster published-half-tile counters, zero on entry
     uint32_t *err;
-    unsigned long long *trace;   // stamps, or null
-    int B, Np, d, f, fpad, W, act, per_token;
-    int P;                       // ring stages
-    int nkb;                     // 64-wide K blocks per gate/up stage (row run = 128 * nkb bytes)
-    int ns;                      // neurons per down stage (64 or 128)
-    int debug;                   // profiling knobs (SPB_TC_DEBUG): 1 no MMAs, 2 no weight copies
-    int force_sk;                // profiling knob (SPB_TC_SK): K-split per tile, 0 = automatic
-    uint32_t stage_bytes;
+    unsigned long long *trace;   // phase stamps, or null
+    int B, Np, d, f, W, fpad, act, per_token;
+    int nu;                      // ring units
+    int gw;                      // units per gate/up stage (1 or 2; nu is even when 2)
+    int nkb;                     // 64-wide K blocks per gate/up stage
+    int nbuf;                    // TMEM accumulator buffers of 2 Np columns
+    int KC;                      // union chunks of the down phase
+    int max_gu, max_dn;          // capacities of the id tables
+    int xdsm;                    // 1: the pair exchanges through distributed shared memory
+    uint32_t unit_bytes;
+    uint64_t timeout_ns;
+    uint32_t hint_acc, hint;     // suspend-time hints of the accumulator / ring waits (ns)
+    int inject;                  // test hook: 1 = CTA rank 1 never signals its results;
+                                 // profiling only: 2 = no output reductions, 4 = no W_down copies
 };
 
 // TMA descriptors of the activations and of h (box 64 x Np, 128-byte swizzle).
@@ -122,105 +140,43 @@ struct TcMaps {
 
 // Phase stamps written when tracing is enabled (spb_trace_enable).
 enum TraceSlot {
-    kTrStart = 0,        // after the dependency wait
-    kTrScanned = 1,      // union scanned, ids emitted
-    kTrGuIssued = 2,     // producers: last gate/up stage issued
-    kTrGuMmaDone = 3,    // MMA: last gate/up stage issued + committed
-    kTrGuAcc = 4,        // epilogue: gate/up accumulators ready
-    kTrGuPublished = 5,  // epilogue: h written / partial handed off
-    kTrFirstFlag = 6,    // producers: h tiles of the first down stage available
-    kTrDnIssued = 7,     // producers: last down stage issued
-    kTrDnAcc = 8,        // epilogue: last down accumulator ready
-    kTrEnd = 9,          // before TMEM release
-    kTrBits = 10,        // union words copied to shared memory
-    kTrScan = 11,        // scan done
-    kTrGuIds = 12,       // gate/up tile ids emitted
-    kTrDnIds = 13,       // down chunk ids emitted
+    kTrStart = 0,       // after the dependency wait
+    kTrScanned = 1,     // union scanned, ids emitted
+    kTrGuIssued = 2,    // producers: all gate/up stages issued
+    kTrGuMmaDone = 3,   // MMA: last gate/up tile committed
+    kTrGuAcc = 4,       // epilogue: first tile's accumulator ready
+    kTrXchg = 5,        // epilogue: partner's half arrived (first tile)
+    kTrHDone = 6,       // epilogue: last tile's h published
+    kTrFirstFlag = 7,   // producers: h of the first down stage available
+    kTrDnIssued = 8,    // producers: all stages issued
+    kTrDnAcc = 9,       // epilogue: down accumulator ready
+    kTrEnd = 10,        // before TMEM release
+    kTrPhase0 = 11,     // phase-0 work done, before the grid barrier
+    kTrBarrier = 12,    // past the grid barrier
+    kTrScan = 13,       // union scanned
+    kTrEmitGu = 14,     // gate/up ids emitted (thread 0's share)
+    kTrEmitDn = 15,     // down ids emitted (thread 0's share)
 };
 constexpr int kTraceSlots = 16;
-// Per-stage stamps of CTA 0: [stage][4] = producer past its empty wait,
-// producer done issuing, (unused), MMA thread sees the stage full.
-constexpr int kStageTraceBase = 160 * kTraceSlots;
+// Per-unit stamps of CTA 0: [unit][4] = MMA issuer: first stage full,
+// committed; epilogue: accumulator seen, released.
+constexpr int kUnitTraceBase = 160 * kTraceSlots;
+constexpr int kUnitTraceMax = 128;
+// Per-stage stamps of CTA 0: [stage][4] = leader past the empty wait, leader
+// done issuing, MMA issuer saw the stage complete.
+constexpr int kStageTraceBase = kUnitTraceBase + kUnitTraceMax * 4;
 constexpr int kStageTraceMax = 256;
+
+__device__ __forceinline__ void stage_stamp(const TcArgs &a, int stage, int what) {
+    if (a.trace && blockIdx.x == 0 && stage < kStageTraceMax) a.trace[kStageTraceBase + stage * 4 + what] = globaltimer();
+}
 
 __device__ __forceinline__ void stamp(const TcArgs &a, int slot) {
     if (a.trace) a.trace[(size_t)blockIdx.x * kTraceSlots + slot] = globaltimer();
 }
 
-__device__ __forceinline__ void stage_stamp(const TcArgs &a, int stage, int what) {
-    if (a.trace && blockIdx.x == 0 && stage < kStageTraceMax)
-        a.trace[kStageTraceBase + stage * 4 + what] = globaltimer();
-}
-
-__device__ __forceinline__ Plan make_plan(int U, int d, int nkb, int grid, int force_sk) {
-    Plan p;
-    p.U = U;
-    p.T = (U + kTileM - 1) / kTileM;
-    p.KG = d / (64 * nkb);
-    p.Sk = p.T ? max(1, min(min(8, p.KG), grid / p.T)) : 1;
-    if (force_sk > 0 && p.T) p.Sk = max(1, min(min(force_sk, p.KG), kMaxGuUnits * grid / p.T));
-    p.ngu = p.T * p.Sk;
-    p.MT = d / kDnCols;
-    p.KC = p.T ? max(1, min(p.T, grid / p.MT)) : 0;
-    p.ndn = p.MT * p.KC;
-    return p;
-}
-
-struct Unit {
-    int kind;              // 0 gate/up, 1 down, -1 none
-    int tile, kg0, kg1;    // gate/up: tile and K-group range
-    int mt, P0, P1;        // down: 256-column slice and union positions [P0, P1)
-    int stages;
-};
-
-__device__ __forceinline__ int num_gu_units(const Plan &p, int c, int grid) {
-    return p.ngu > c ? (p.ngu - c + grid - 1) / grid : 0;
-}
-
-// The u-th unit of CTA c: gate/up items c, c+grid, ... then its down item
-// (there is at most one: ndn <= grid).
-__device__ __forceinline__ Unit unit_of(const Plan &p, int c, int grid, int u, int ns) {
-    Unit x{};
-    x.kind = -1;
-    const int n_gu = num_gu_units(p, c, grid);
-    if (u < n_gu) {
-        const int g = c + u * grid;
-        const int ks = g % p.Sk;
-        x.kind = 0;
-        x.tile = g / p.Sk;
-        x.kg0 = ks * p.KG / p.Sk;
-        x.kg1 = (ks + 1) * p.KG / p.Sk;
-        x.stages = x.kg1 - x.kg0;  // one K group (gate + up rows) per stage
-        return x;
-    }
-    if (u == n_gu && c < p.ndn) {
-        const int kc = c / p.MT;
-        x.kind = 1;
-        x.mt = c % p.MT;
-        x.P0 = (p.T * kc / p.KC) * kTileM;
-        x.P1 = min(p.U, (p.T * (kc + 1) / p.KC) * kTileM);
-        x.stages = x.P1 > x.P0 ? (x.P1 - x.P0 + ns - 1) / ns : 0;
-    }
-    return x;
-}
-
-// Writes the neuron ids of union positions [P0, P1) to out[p - P0] (the whole
-// block cooperates, one 32-neuron word per thread); out[i] for
-// P1 - P0 <= i < n is set to `fill`.
-__device__ __forceinline__ void emit_ids(const uint32_t *bits, const int *prefix, int W, int P0, int P1, int n,
-                                         int fill, int *out) {
-    for (int i = max(P1 - P0, 0) + (int)threadIdx.x; i < n; i += blockDim.x) out[i] = fill;
-    for (int w = threadIdx.x; w < W; w += blockDim.x) {
-        int p = prefix[w];
-        if (prefix[w + 1] <= P0 || p >= P1) continue;
-        uint32_t word = bits[w];
-        while (word) {
-            const int b = __ffs(word) - 1;
-            word &= word - 1;
-            if (p >= P0 && p < P1) out[p - P0] = w * 32 + b;
-            ++p;
-        }
-    }
+__device__ __forceinline__ void unit_stamp(const TcArgs &a, int unit, int what) {
+    if (a.trace && blockIdx.x == 0 && unit < kUnitTraceMax) a.trace[kUnitTraceBase + unit * 4 + what] = globaltimer();
 }
 
 __device__ __forceinline__ void raise_error(uint32_t *err, TcCtl *ctl, uint32_t code) {
@@ -230,33 +186,54 @@ __device__ __forceinline__ void raise_error(uint32_t *err, TcCtl *ctl, uint32_t 
 
 // Bounded mbarrier wait; false on timeout or abort.  `hint_ns` is how long a
 // waiting thread may sleep between checks (it wakes on completion).
-__device__ __forceinline__ bool wait_bar(uint64_t *bar, uint32_t parity, TcCtl *ctl, uint32_t *err, uint32_t code,
+__device__ __forceinline__ bool wait_bar(uint64_t *bar, uint32_t parity, TcCtl *ctl, const TcArgs &a, uint32_t code,
                                          uint32_t hint_ns) {
     if (mbar_test(bar, parity)) return true;
     const uint64_t t0 = globaltimer();
     while (!mbar_test_sleep(bar, parity, hint_ns)) {
         if (ctl->abort) return false;
-        if (globaltimer() - t0 > kTimeoutNs) {
-            raise_error(err, ctl, code);
+        if (globaltimer() - t0 > a.timeout_ns) {
+            raise_error(a.err, ctl, code);
             return false;
         }
     }
     return true;
 }
 
-// Bounded wait for a gate/up tile's ready flag.
-__device__ __forceinline__ bool wait_flag(const uint32_t *flag, TcCtl *ctl, uint32_t *err) {
-    if (ld_acquire_u32(flag) != 0) return true;
+// The same for barriers the partner CTA arrives on (acquire at cluster scope).
+__device__ __forceinline__ bool wait_bar_cluster(uint64_t *bar, uint32_t parity, TcCtl *ctl, const TcArgs &a,
+                                                 uint32_t code) {
     const uint64_t t0 = globaltimer();
-    while (ld_acquire_u32(flag) == 0) {
+    while (!mbar_test_cluster(bar, parity, 2000)) {
         if (ctl->abort) return false;
-        if (globaltimer() - t0 > kTimeoutNs) {
-            raise_error(err, ctl, kErrTimeoutFlag);
+        if (globaltimer() - t0 > a.timeout_ns) {
+            raise_error(a.err, ctl, code);
             return false;
         }
-        __nanosleep(256);
     }
     return true;
+}
+
+// Bounded wait until a cluster's counter reaches `target` (acquire, GPU scope).
+__device__ __forceinline__ bool wait_count(const uint32_t *cnt, uint32_t target, TcCtl *ctl, const TcArgs &a) {
+    if (ld_acquire_u32(cnt) >= target) return true;
+    const uint64_t t0 = globaltimer();
+    while (ld_acquire_u32(cnt) < target) {
+        if (ctl->abort) return false;
+        if (globaltimer() - t0 > a.timeout_ns) {
+            raise_error(a.err, ctl, kErrTimeoutFlag);
+            return false;
+        }
+        __nanosleep(128);
+    }
+    return true;
+}
+
+// The ring: stages occupy consecutive units in round robin; unit-step t
+// (the t-th unit occupied in this launch) is unit t % NU and completes phase
+// t / NU of that unit's barriers.
+__device__ __forceinline__ bool ring_wait_empty(int t, int NU, TcCtl *ctl, const TcArgs &a) {
+    return t < NU || wait_bar(&ctl->empty[t % NU], (uint32_t)(t / NU - 1) & 1u, ctl, a, kErrTimeoutEmpty, a.hint);
 }
 
 __device__ __forceinline__ float act_h(float g, float u, int act) {
@@ -264,335 +241,587 @@ __device__ __forceinline__ float act_h(float g, float u, int act) {
     return act == SPB_ACT_RELU_RELU_MUL ? g * fmaxf(u, 0.0f) : g * u;
 }
 
+// First union position of cluster c of C (U positions in all; U <= 32768 and
+// C <= 80, so the product fits 32 bits).
+__device__ __forceinline__ int cluster_start(int U, int c, int C) { return (int)((uint32_t)(U * c) / (uint32_t)C); }
+
+// Rows [r0, r1) of tile i when a cluster's n positions are cut into nt
+// near-equal tiles of at most 128.
+__device__ __forceinline__ void tile_rows(int n, int nt, int i, int &r0, int &r1) {
+    r0 = (int)((uint32_t)(n * i) / (uint32_t)nt);
+    r1 = (int)((uint32_t)(n * (i + 1)) / (uint32_t)nt);
+}
+
+__device__ __forceinline__ int tiles_of(int n) { return (n + kTileM - 1) / kTileM; }
+
+// Union chunk k of KC for the down phase: 64-aligned start, so the h tiles'
+// TMA coordinates are 16-byte aligned.
+__device__ __forceinline__ int chunk_start(int U, int k, int KC) {
+    if (k >= KC) return U;
+    return min(U, (int)(((uint32_t)(U * k) / (uint32_t)KC + 63u) & ~63u));
+}
+
+// The word holding union position p (0 <= p < U): the largest w with
+// prefix[w] <= p.
+__device__ __forceinline__ int word_of(const int *prefix, int W, int p) {
+    int lo = 0, hi = W - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (prefix[mid] <= p) lo = mid;
+        else hi = mid - 1;
+    }
+    return lo;
+}
+
+// For positions [p0, p1) of the ascending union, writes the neuron ids to
+// out[p - p0] (16-bit: f <= 32768).  Warps `warp0 + i * nwarps` take one
+// 32-neuron word each, every lane placing its own bit by its rank in the
+// word; only the words that hold the range are visited.
+__device__ __forceinline__ void emit_ids16(const uint32_t *bits, const int *prefix, int W, int p0, int p1,
+                                           uint16_t *out, int warp0, int nwarps) {
+    if (p1 <= p0) return;
+    const int lane = threadIdx.x & 31;
+    const int w0 = word_of(prefix, W, p0), w1 = word_of(prefix, W, p1 - 1);
+    for (int w = w0 + warp0; w <= w1; w += nwarps) {
+        const uint32_t word = bits[w];
+        if ((word >> lane) & 1u) {
+            const int p = prefix[w] + __popc(word & ((1u << lane) - 1u));
+            if (p >= p0 && p < p1) out[p - p0] = (uint16_t)(w * 32 + lane);
+        }
+    }
+}
+
 __global__ void __launch_bounds__(kTcThreads, 1)
 ffn_tc_kernel(const __grid_constant__ TcMaps maps, const TcArgs a) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    const int P = a.P, W = a.W, Np = a.Np, nkb = a.nkb, ns = a.ns;
+    const int NU = a.nu, GW = a.gw, W = a.W, Np = a.Np, nkb = a.nkb, nbuf = a.nbuf;
     uint8_t *ring = smem;
-    TcCtl *ctl = reinterpret_cast<TcCtl *>(ring + (size_t)P * a.stage_bytes);
-    // prologue-only tables live in the ring, which no copy touches before the
-    // ids are emitted
-    int *prefix = reinterpret_cast<int *>(ring);               // [W + 1]
-    int *wtot = prefix + W + 1;                                // [64]
-    uint32_t *bits = reinterpret_cast<uint32_t *>(wtot + 64);  // [W]
-    int *gu_ids = reinterpret_cast<int *>(ctl + 1);            // [kMaxGuUnits][128]
-    int *dn_ids = gu_ids + kMaxGuUnits * kTileM;               // [max_chunk]
+    TcCtl *ctl = reinterpret_cast<TcCtl *>(ring + (size_t)NU * a.unit_bytes);
+    uint32_t *tokmask = reinterpret_cast<uint32_t *>(ctl + 1);  // [8][128] per tile row: its tokens' bits
+    uint16_t *gu_ids = reinterpret_cast<uint16_t *>(tokmask + 8 * kTileM);  // [max_gu]
+    uint16_t *dn_ids = gu_ids + a.max_gu;                                    // [max_dn]
+    // [Np][64] fp32: the partner's results for this CTA's rows, when they
+    // travel through distributed shared memory (a.xdsm)
+    float *xrecv = reinterpret_cast<float *>(reinterpret_cast<uintptr_t>(dn_ids + a.max_dn + 3) & ~uintptr_t(15));
+    // union tables: the down ids are emitted from them while the gate/up
+    // stages stream
+    int *prefix = reinterpret_cast<int *>(xrecv + (a.xdsm ? 64 * Np : 0));  // [W + 1]
+    int *wtot = prefix + W + 1;                                              // [64]
+    uint32_t *bits = reinterpret_cast<uint32_t *>(wtot + 64);                // [W]
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const uint32_t ncols = Np * 2 <= 32 ? 32 : (Np * 2 <= 64 ? 64 : (Np * 2 <= 128 ? 128 : (Np * 2 <= 256 ? 256 : 512)));
+    const uint32_t rank = cluster_ctarank(), peer = rank ^ 1u;
+    const int clu = blockIdx.x >> 1, nclu = gridDim.x >> 1;
 
     if (tid == 0) {
-        for (int i = 0; i < P; ++i) {
-            mbar_init(&ctl->full[i], kProducerWarps * 32 + 1);  // producer cp.async arrivals + 1 TMA expect_tx arrival
+        for (int i = 0; i < NU; ++i) {
+            mbar_init(&ctl->full[i], kProducerThreads);
+            mbar_init(&ctl->tma[i], 1);
             mbar_init(&ctl->empty[i], 1);
         }
-        mbar_init(&ctl->acc_full, 1);
-        mbar_init(&ctl->acc_empty, 128);
+        for (int i = 0; i < nbuf; ++i) {
+            mbar_init(&ctl->acc_full[i], 1);
+            mbar_init(&ctl->acc_empty[i], kEpiWarps * 32);
+        }
+        mbar_init(&ctl->xchg_full, kEpiWarps * 32);
+        mbar_init(&ctl->xchg_free, kEpiWarps * 32);
+        mbar_init(&ctl->ids_ready, kEpiWarps * 32);
         ctl->abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    if (warp == kMmaWarp) tmem_alloc(&ctl->tmem_base, ncols);
+    if (warp == kMmaWarp) tmem_alloc(&ctl->tmem_base, kTmemCols);
+    // the partner may arrive on this CTA's barriers only once they exist
+    cluster_sync_all();
 
-    // Inputs written by the union launch become visible here.
+    // Whatever the previous kernel on the stream wrote (these inputs, this
+    // workspace) becomes visible here.
     grid_dependency_wait();
     if (tid == 0) stamp(a, kTrStart);
-    for (int w = tid; w < W; w += kTcThreads) bits[w] = a.seg_bits[w];
+    // ---- phase 0, shared by all CTAs: union bits, fp16 activations, zeroed
+    // output and counters; then one grid barrier.
+    {
+        const int64_t gt = (int64_t)blockIdx.x * kTcThreads + tid, gs = (int64_t)gridDim.x * kTcThreads;
+        const int64_t n2 = (int64_t)Np * a.d / 2;
+        // the first two activation pairs of this thread are loaded before the
+        // label reads, so both wait on memory together
+        float2 xv0 = make_float2(0.f, 0.f), xv1 = make_float2(0.f, 0.f);
+        if (gt < n2 && (int)((2 * gt) / a.d) < a.B) xv0 = *reinterpret_cast<const float2 *>(a.x + 2 * gt);
+        if (gt + gs < n2 && (int)((2 * (gt + gs)) / a.d) < a.B) xv1 = *reinterpret_cast<const float2 *>(a.x + 2 * (gt + gs));
+        // word w is handled by CTA w % grid, so every SM shares the label reads
+        const int gwarps = gridDim.x * kTcWarps;
+        for (int w = warp * gridDim.x + blockIdx.x; w < W; w += gwarps) {
+            const int j = w * 32 + lane;
+            const bool in = j < a.f;
+            uint32_t seg = 0;
+            if (a.tok_in) {
+                for (int t = lane; t < a.B; t += 32) {
+                    const uint32_t b = a.tok_in[(int64_t)t * W + w] & (w == W - 1 && (a.f & 31) ? (1u << (a.f & 31)) - 1u : ~0u);
+                    a.tok_bits[(int64_t)t * W + w] = b;
+                    seg |= b;
+                }
+                seg = __reduce_or_sync(0xffffffffu, seg);
+            } else {
+                for (int t0 = 0; t0 < a.B; t0 += 32) {
+                    // every token of a 32-token group in flight at once
+                    float v[32];
+#pragma unroll
+                    for (int q = 0; q < 32; ++q) v[q] = (in && t0 + q < a.B) ? __ldg(a.labels + (int64_t)(t0 + q) * a.f + j) : 0.0f;
+#pragma unroll
+                    for (int q = 0; q < 32; ++q) {
+                        const uint32_t b = __ballot_sync(0xffffffffu, v[q] > 0.0f);
+                        if (lane == q && t0 + q < a.B) a.tok_bits[(int64_t)(t0 + q) * W + w] = b;
+                        seg |= b;
+                    }
+                }
+            }
+            if (lane == 0) a.seg_bits[w] = seg;
+        }
+        if (gt < n2) reinterpret_cast<__half2 *>(a.x16)[gt] = __floats2half2_rn(xv0.x, xv0.y);
+        if (gt + gs < n2) reinterpret_cast<__half2 *>(a.x16)[gt + gs] = __floats2half2_rn(xv1.x, xv1.y);
+        for (int64_t i = gt + 2 * gs; i < n2; i += gs) {
+            const int t = (int)((2 * i) / a.d);
+            const float2 v = t < a.B ? *reinterpret_cast<const float2 *>(a.x + 2 * i) : make_float2(0.f, 0.f);
+            reinterpret_cast<__half2 *>(a.x16)[i] = __floats2half2_rn(v.x, v.y);
+        }
+        const int64_t n4 = (int64_t)a.B * a.d / 4;
+        for (int64_t i = gt; i < n4; i += gs) reinterpret_cast<float4 *>(a.out)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (gt < nclu) a.ready[gt] = 0u;
+        if (tid == 0) stamp(a, kTrPhase0);
+        // grid barrier: gbar[0] counts arrivals (zero on entry); the last CTA
+        // to leave resets both words for the next launch
+        __syncthreads();
+        if (tid == 0) {
+            __threadfence();
+            red_add_release_u32(a.gbar, 1u);
+            const uint64_t t0 = globaltimer();
+            while (ld_acquire_u32(a.gbar) < gridDim.x) {
+                if (globaltimer() - t0 > a.timeout_ns) {
+                    raise_error(a.err, ctl, kErrTimeoutGrid);
+                    break;
+                }
+                __nanosleep(32);
+            }
+            if (atomicAdd(a.gbar + 1, 1u) == gridDim.x - 1) {
+                a.gbar[0] = 0u;
+                a.gbar[1] = 0u;
+            }
+        }
+        __syncthreads();
+    }
+    if (tid == 0) stamp(a, kTrBarrier);
+    for (int w = tid; w < W; w += kTcThreads) bits[w] = __ldcg(a.seg_bits + w);
     __syncthreads();
-    if (tid == 0) stamp(a, kTrBits);
     scan_popc(bits, W, prefix, wtot);  // ends with __syncthreads
     if (tid == 0) stamp(a, kTrScan);
-    const int grid = gridDim.x, c = blockIdx.x;
-    const Plan pl = make_plan(prefix[W], a.d, nkb, grid, a.force_sk);
-    if (c == 0 && tid == 0) *a.count_out = pl.U;
-    const int n_gu = min(num_gu_units(pl, c, grid), kMaxGuUnits);
-    const int nunits = n_gu + (c < pl.ndn ? 1 : 0);
-    // neuron ids of this CTA's tiles and down chunk; a.f (out of range) marks
-    // padding rows, which are zero-filled
-    for (int u = 0; u < n_gu; ++u) {
-        const Unit un = unit_of(pl, c, grid, u, ns);
-        emit_ids(bits, prefix, W, un.tile * kTileM, min(pl.U, un.tile * kTileM + kTileM), kTileM, a.f,
-                 gu_ids + u * kTileM);
-    }
-    if (tid == 0) stamp(a, kTrGuIds);
-    const Unit dn = unit_of(pl, c, grid, n_gu, ns);
-    if (dn.kind == 1) emit_ids(bits, prefix, W, dn.P0, dn.P1, dn.stages * ns, a.f, dn_ids);
-    if (tid == 0) stamp(a, kTrDnIds);
+    const int U = prefix[W];
+    // gate/up work of this cluster
+    const int P0 = cluster_start(U, clu, nclu);
+    const int n = cluster_start(U, clu + 1, nclu) - P0;
+    const int ntile = tiles_of(n);
+    // down unit of this CTA: 256-column slice m of union chunk k
+    const int MT = a.d / kSlice;
+    const int unit = blockIdx.x;
+    const bool has_dn = unit < MT * a.KC;
+    const int m = unit % MT, k = unit / MT;
+    const int Q0 = has_dn ? chunk_start(U, k, a.KC) : 0;
+    const int Q1 = has_dn ? chunk_start(U, k + 1, a.KC) : 0;
+    const int ndn = (Q1 - Q0 + kDnRows - 1) / kDnRows;  // down stages
+    if (blockIdx.x == 0 && tid == 0) *a.count_out = U;
+    emit_ids16(bits, prefix, W, P0, P0 + n, gu_ids, warp, kTcWarps);
+    if (tid == 0) stamp(a, kTrEmitGu);
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = ctl->tmem_base;
     if (tid == 0) stamp(a, kTrScanned);
+    // The next launch on the stream may be scheduled now; it waits for this
+    // grid to finish before it touches anything.
+    if (tid == 0) grid_launch_dependents();
 
-    if (warp >= kProducerWarp0 && warp < kProducerWarp0 + kProducerWarps) {
+    const int KG = a.d / (64 * nkb);
+
+    if (warp >= kProducerWarp0 && warp < kMmaWarp) {
         // ------------------------------------------------------------ producers
         const int pt = tid - kProducerWarp0 * 32, pw = pt >> 5;
-        const bool leader = pt == 0;
-        const bool copy_w = !(a.debug & 2);
-        int s = 0;
-        for (int u = 0; u < nunits; ++u) {
-            const Unit un = unit_of(pl, c, grid, u, ns);
-            bool ok = true;
-            int flag_next = un.kind == 1 ? un.P0 / kTileM : 0;  // first gate/up tile not yet seen ready
-            // CTAs sharing a K range start at different K groups: rows are 8 KB
-            // apart, so CTAs stepping through the same column window in lock
-            // step would all hit the same few DRAM channels.
-            const int nk = un.kind == 0 ? un.kg1 - un.kg0 : 1;  // K groups of the unit
-            const int rot = un.kind == 0 && nk > 0 ? (un.tile % nk) : 0;
-            for (int st = 0; st < un.stages; ++st, ++s) {
-                const int slot = s % P, round = s / P;
-                ok = round == 0 || wait_bar(&ctl->empty[slot], (round - 1) & 1, ctl, a.err, kErrTimeoutEmpty, 1000);
-                if (!ok) break;
-                uint64_t *bar = &ctl->full[slot];
-                const uint32_t sbase = smem_u32(ring + (size_t)slot * a.stage_bytes);
+        const bool leader = pt == 0;  // stamps only
+        const __half *wm = rank ? a.wu : a.wg;
+        const int rot = KG ? clu % KG : 0;  // spreads the clusters' column windows over DRAM
+        const int cpr = nkb * 8;            // 16-byte chunks per row run
+        const int rpw = 32 / cpr;           // rows per warp instruction
+        const int ch = lane & (cpr - 1), kbl = ch >> 3, cc = ch & 7;
+        bool ok = !ctl->abort;
+        int s = 0, t = 0;  // stage index (for stamps), unit-step
+        for (int i = 0; i < ntile && ok; ++i) {
+            int r0, r1;
+            tile_rows(n, ntile, i, r0, r1);
+            const int rows = r1 - r0;
+            const uint16_t *tids = gu_ids + r0;
+            for (int st = 0; st < KG; ++st, ++s, t += GW) {
+                if (!(ok = ring_wait_empty(t, NU, ctl, a) && (GW == 1 || ring_wait_empty(t + 1, NU, ctl, a)))) break;
+                const uint32_t sbase = smem_u32(ring + (size_t)(t % NU) * a.unit_bytes);
+                const int kbase = ((st + rot) % KG) * 64 * nkb;
                 if (leader) stage_stamp(a, s, 0);
-                if (un.kind == 0) {
-                    // one K group: gate and up rows (nkb x 128 B each) + the activations
-                    const int kbase = (un.kg0 + (st + rot) % nk) * 64 * nkb;
-                    if (leader) {  // activations: nkb TMA tiles of 64 columns x Np rows
-                        mbar_arrive_expect_tx(bar, (uint32_t)nkb * Np * 128);
-                        for (int kbl = 0; kbl < nkb; ++kbl)
-                            tma_load_2d(sbase + 2 * nkb * kATile + kbl * Np * 128, &maps.x, bar, kbase + kbl * 64, 0);
-                    }
-                    // weights: 128 rows x (nkb x 128 B) per matrix; each warp
-                    // instruction copies whole row runs
-                    const int cpr = nkb * 8;    // 16-byte chunks per row run
-                    const int rpw = 32 / cpr;   // rows per warp instruction
-                    const int ch = lane & (cpr - 1), kbl = ch >> 3, cc = ch & 7;
-                    if (copy_w) {
-#pragma unroll
-                        for (int m = 0; m < 2; ++m) {
-                            const __half *wl = (m ? a.wu : a.wg) + kbase + ch * 8;
-                            const uint32_t dl = sbase + (m * nkb + kbl) * kATile + (uint32_t)cc * 16;
-                            for (int r = pw * rpw + lane / cpr; r < 128; r += kProducerWarps * rpw) {
-                                const int j = gu_ids[u * kTileM + r];
-                                // padding rows past the union copy row 0: the epilogue
-                                // zeroes h for them, so their products are never used
-                                cp_async16_full((dl + r * 128) ^ ((uint32_t)(r & 7) << 4),
-                                                wl + (int64_t)(j < a.f ? j : 0) * a.d);
-                            }
-                        }
-                    }
-                } else {
-                    const int p0s = un.P0 + st * ns;
-                    // W_down rows as the MN-major operand: ns neurons x 256
-                    // columns (32 chunks), one row per warp.  They do not depend
-                    // on the gate/up phase, so they are copied at once; only h
-                    // waits for its tiles below.
-                    const int m0 = un.mt * kDnCols;
-                    const uint32_t lbo = (uint32_t)(ns / 8) * 1024;
-                    const int mb = lane >> 3, cc = lane & 7;
-                    if (copy_w) {
-                        for (int kk = pw; kk < ns; kk += kProducerWarps) {
-                            const int j = dn_ids[(p0s - un.P0) + kk];
-                            const int kg = kk >> 3, kr = kk & 7;
-                            cp_async16(sbase + mb * lbo + kg * 1024 + kr * 128 + ((cc ^ kr) << 4),
-                                       a.wd + (int64_t)(j < a.f ? j : 0) * a.d + m0 + lane * 8, j < a.f ? 16u : 0u);
-                        }
-                    }
-                    if (leader) {
-                        // h of this stage's neurons: wait for the gate/up tiles
-                        // that hold them (published by other CTAs), then TMA
-                        // ns/64 tiles of 64 neurons x Np tokens.
-                        const int t1 = (min(p0s + ns, un.P1) - 1) / kTileM;
-                        for (; flag_next <= t1 && ok; ++flag_next) ok = wait_flag(a.tile_ready + flag_next, ctl, a.err);
-                        if (st == 0) stamp(a, kTrFirstFlag);
-                        // the h stores were made through the generic proxy;
-                        // the TMA below reads through the async proxy
-                        asm volatile("fence.proxy.async.global;" ::: "memory");
-                        mbar_arrive_expect_tx(bar, (uint32_t)(ns / 64) * Np * 128);
-                        for (int kbl = 0; kbl < ns / 64; ++kbl)
-                            tma_load_2d(sbase + (uint32_t)ns * 512 + kbl * Np * 128, &maps.h, bar, p0s + kbl * 64, 0);
-                    }
-                }
-                cp_async_mbar_arrive(bar);
+                // weight rows: rows x (nkb x 128 B); rows past the tile are not
+                // copied (their MMA rows are never read)
+                const uint32_t dl = sbase + kbl * kATile + (uint32_t)cc * 16;
+                const __half *src = wm + kbase + ch * 8;
+                for (int r = pw * rpw + lane / cpr; r < rows; r += kProducerWarps * rpw)
+                    cp_async16_full((dl + r * 128) ^ ((uint32_t)(r & 7) << 4), src + (int64_t)tids[r] * a.d);
+                cp_async_mbar_arrive(&ctl->full[t % NU]);
+                if (GW == 2) cp_async_mbar_arrive(&ctl->full[(t + 1) % NU]);
                 if (leader) stage_stamp(a, s, 1);
             }
-            if (!ok) break;
-            if (leader) stamp(a, un.kind == 0 ? kTrGuIssued : kTrDnIssued);
         }
+        if (leader) stamp(a, kTrGuIssued);
+        // Down stages: W_down rows (64 positions x 256 columns, MN-major:
+        // 64-column blocks kDnLbo apart, 8-row K groups 1024 B apart; rows past
+        // the chunk up to the next multiple of 16 zero-filled) are copied at
+        // once; the TMA warp adds the h tile once its producers published it.
+        const int mb = lane >> 3, c8 = lane & 7;
+        const int cbase = m * kSlice;
+        if (ok && ndn > 0) ok = wait_bar(&ctl->ids_ready, 0, ctl, a, kErrTimeoutAcc, a.hint);
+        for (int st = 0; st < ndn && ok; ++st, ++s, ++t) {
+            if (!(ok = ring_wait_empty(t, NU, ctl, a))) break;
+            const uint32_t sbase = smem_u32(ring + (size_t)(t % NU) * a.unit_bytes);
+            const int p0 = Q0 + st * kDnRows;
+            const int nr = min(kDnRows, Q1 - p0), nr16 = (nr + 15) & ~15;
+            if (leader) stage_stamp(a, s, 0);
+            for (int kk = pw; kk < (a.inject == 4 ? 0 : nr16); kk += kProducerWarps) {
+                const bool valid = kk < nr;
+                const int j = valid ? dn_ids[p0 - Q0 + kk] : 0;
+                const int kg = kk >> 3, kr = kk & 7;
+                cp_async16(sbase + mb * kDnLbo + kg * 1024 + kr * 128 + ((c8 ^ kr) << 4),
+                           a.wd + (int64_t)j * a.d + cbase + lane * 8, valid ? 16u : 0u);
+            }
+            if (leader) stage_stamp(a, s, 1);
+            cp_async_mbar_arrive(&ctl->full[t % NU]);
+        }
+        if (leader) stamp(a, kTrDnIssued);
+        // Every copy this thread issued lands before the CTA can exit.
+        cp_async_wait_all();
+    } else if (warp == kTmaWarp) {
+        // ------------------------------------------------------------ TMA issue
+        // One thread streams the activation tiles of the gate/up stages and
+        // the h tiles of the down stages into the ring, each on its slot's
+        // transaction barrier.
+        if (lane == 0) {
+            int t = 0;  // unit-step
+            // x16 was written by generic stores in phase 0; TMA reads through
+            // the async proxy
+            asm volatile("fence.proxy.async.global;" ::: "memory");
+            const int rot = KG ? clu % KG : 0;
+            bool ok = !ctl->abort;
+            for (int i = 0; i < ntile && ok; ++i) {
+                for (int st = 0; st < KG; ++st, t += GW) {
+                    if (!(ok = ring_wait_empty(t, NU, ctl, a) && (GW == 1 || ring_wait_empty(t + 1, NU, ctl, a))))
+                        break;
+                    const uint32_t sbase = smem_u32(ring + (size_t)(t % NU) * a.unit_bytes);
+                    const int kbase = ((st + rot) % KG) * 64 * nkb;
+                    uint64_t *bar = &ctl->tma[t % NU];
+                    mbar_arrive_expect_tx(bar, (uint32_t)nkb * Np * 128);
+                    if (GW == 2) mbar_arrive(&ctl->tma[(t + 1) % NU]);
+                    for (int kb = 0; kb < nkb; ++kb)
+                        tma_load_2d(sbase + nkb * kATile + kb * Np * 128, &maps.x, bar, kbase + kb * 64, 0);
+                }
+            }
+            // clusters [.., cl_ok) are known to have published all their h
+            int cl_ok = 0;
+            while (cl_ok + 1 < nclu && cluster_start(U, cl_ok + 1, nclu) <= Q0) ++cl_ok;
+            for (int st = 0; st < ndn && ok; ++st, ++t) {
+                if (!(ok = ring_wait_empty(t, NU, ctl, a))) break;
+                const int p0 = Q0 + st * kDnRows;
+                const int nr16 = (min(kDnRows, Q1 - p0) + 15) & ~15;
+                // h of positions [p0, p0 + nr16): wait for every cluster that
+                // owns one of them and has not been confirmed yet
+                const int last = min(p0 + nr16, U) - 1;
+                bool fresh = false;
+                while (ok && cl_ok < nclu && cluster_start(U, cl_ok, nclu) <= last) {
+                    const int cn = cluster_start(U, cl_ok + 1, nclu) - cluster_start(U, cl_ok, nclu);
+                    ok = wait_count(a.ready + cl_ok, 2u * (uint32_t)tiles_of(cn), ctl, a);
+                    fresh = true;
+                    ++cl_ok;
+                }
+                if (!ok) break;
+                if (st == 0) stamp(a, kTrFirstFlag);
+                // h was stored through the generic proxy; TMA reads through
+                // the async proxy
+                if (fresh) asm volatile("fence.proxy.async.global;" ::: "memory");
+                const uint32_t sbase = smem_u32(ring + (size_t)(t % NU) * a.unit_bytes);
+                mbar_arrive_expect_tx(&ctl->tma[t % NU], (uint32_t)Np * 128);
+                tma_load_2d(sbase + kDnWBytes, &maps.h, &ctl->tma[t % NU], p0, 0);
+            }
+            // Every TMA this thread issued lands before the CTA can exit: the
+            // last NU unit-steps it armed each complete their phase.
+            const uint64_t t0 = globaltimer();
+            for (int q = t - 1; q >= 0 && q >= t - NU; --q)
+                while (!mbar_test_sleep(&ctl->tma[q % NU], (uint32_t)(q / NU) & 1u, 1000) &&
+                       globaltimer() - t0 < a.timeout_ns) {
+                }
+        }
+        __syncwarp();
     } else if (warp == kMmaWarp) {
         // ------------------------------------------------------------ MMA issuer
         if (lane == 0) {
             const uint32_t id_gu = idesc_f16_f32(kTileM, Np, false, false);
             const uint32_t id_dn = idesc_f16_f32(kTileM, Np, true, false);
-            const uint32_t lbo = (uint32_t)(ns / 8) * 1024;
-            const bool do_mma = !(a.debug & 1);
-            int s = 0;
-            for (int u = 0; u < nunits && !ctl->abort; ++u) {
-                const Unit un = unit_of(pl, c, grid, u, ns);
-                if (u > 0 && !wait_bar(&ctl->acc_empty, (u - 1) & 1, ctl, a.err, kErrTimeoutAcc, 2000)) break;
+            uint64_t *last_bar = nullptr;  // barrier of the most recent commit, for the drain
+            uint32_t last_par = 0;
+            bool ok = !ctl->abort;
+            int s = 0, ub = 0;
+            auto acquire_buf = [&](int &buf) -> bool {
+                buf = ub % nbuf;
+                const int rnd = ub / nbuf;
+                if (rnd > 0 && !wait_bar(&ctl->acc_empty[buf], (rnd - 1) & 1, ctl, a, kErrTimeoutAcc, a.hint))
+                    return false;
                 tc_fence_after();
-                bool ok = true;
-                for (int st = 0; st < un.stages; ++st, ++s) {
-                    const int slot = s % P, round = s / P;
-                    if (!wait_bar(&ctl->full[slot], round & 1, ctl, a.err, kErrTimeoutFull, 1000)) {
-                        ok = false;
-                        break;
-                    }
-                    stage_stamp(a, s, 3);
-                    // the producers' cp.async data were written through the
-                    // generic proxy; make them visible to the MMA's async proxy
-                    fence_proxy_async_smem();
-                    tc_fence_after();
-                    const uint32_t sbase = smem_u32(ring + (size_t)slot * a.stage_bytes);
-                    if (do_mma && un.kind == 0) {
-                        // gate rows -> TMEM columns [0, Np), up rows -> [Np, 2 Np)
-                        const uint32_t xoff = 2 * nkb * kATile;
-                        for (int kbl = 0; kbl < nkb; ++kbl) {
+                return true;
+            };
+            int t = 0;  // unit-step
+            auto wait_unit = [&](int q) -> bool {
+                const uint32_t par = (uint32_t)(q / NU) & 1u;
+                return wait_bar(&ctl->full[q % NU], par, ctl, a, kErrTimeoutFull, a.hint) &&
+                       wait_bar(&ctl->tma[q % NU], par, ctl, a, kErrTimeoutFull, a.hint);
+            };
+            auto wait_stage = [&](int w) -> bool {
+                if (!wait_unit(t) || (w == 2 && !wait_unit(t + 1))) return false;
+                stage_stamp(a, s, 2);
+                // the producers' cp.async data were written through the
+                // generic proxy; make them visible to the MMA's async proxy
+                fence_proxy_async_smem();
+                tc_fence_after();
+                return true;
+            };
+            auto commit_acc = [&](int buf) {
+                unit_stamp(a, ub, 1);
+                mma_commit(&ctl->acc_full[buf]);
+                last_bar = &ctl->acc_full[buf];
+                last_par = (uint32_t)(ub / nbuf) & 1u;
+                ++ub;
+            };
+            for (int i = 0; i < ntile && ok; ++i) {
+                int buf;
+                if (!(ok = acquire_buf(buf))) break;
+                const uint32_t dgu = tmem + (uint32_t)(buf * 2 * Np);
+                for (int st = 0; st < KG; ++st, ++s, t += GW) {
+                    if (!(ok = wait_stage(GW))) break;
+                    if (st == 0) unit_stamp(a, ub, 0);
+                    const uint32_t sbase = smem_u32(ring + (size_t)(t % NU) * a.unit_bytes);
+                    const uint32_t xoff = sbase + (uint32_t)nkb * kATile;
+                    for (int kb = 0; kb < nkb; ++kb) {
 #pragma unroll
-                            for (int k4 = 0; k4 < 4; ++k4) {
-                                const uint64_t bd = desc_sw128(sbase + xoff + kbl * Np * 128 + k4 * 32, 16, 1024);
-                                const uint32_t acc = (st > 0 || kbl > 0 || k4 > 0) ? 1u : 0u;
-#pragma unroll
-                                for (int m = 0; m < 2; ++m) {
-                                    const uint64_t ad = desc_sw128(sbase + (m * nkb + kbl) * kATile + k4 * 32, 16, 1024);
-                                    mma_f16(tmem + m * Np, ad, bd, id_gu, acc);
-                                }
-                            }
-                        }
-                    } else if (do_mma) {
-                        const uint32_t hoff = (uint32_t)ns * 512;
-                        for (int kbl = 0; kbl < ns / 64; ++kbl) {
-#pragma unroll
-                            for (int k4 = 0; k4 < 4; ++k4) {
-                                const uint64_t bd = desc_sw128(sbase + hoff + kbl * Np * 128 + k4 * 32, 16, 1024);
-                                const uint32_t acc = (st > 0 || kbl > 0 || k4 > 0) ? 1u : 0u;
-#pragma unroll
-                                for (int mt2 = 0; mt2 < 2; ++mt2) {
-                                    const uint64_t ad =
-                                        desc_sw128(sbase + mt2 * 2 * lbo + (kbl * 8 + k4 * 2) * 1024, lbo, 1024);
-                                    mma_f16(tmem + mt2 * Np, ad, bd, id_dn, acc);
-                                }
-                            }
+                        for (int k4 = 0; k4 < 4; ++k4) {
+                            const uint64_t ad = desc_sw128(sbase + kb * kATile + k4 * 32, 16, 1024);
+                            const uint64_t bd = desc_sw128(xoff + kb * Np * 128 + k4 * 32, 16, 1024);
+                            mma_f16(dgu, ad, bd, id_gu, (st > 0 || kb > 0 || k4 > 0) ? 1u : 0u);
                         }
                     }
-                    mma_commit(&ctl->empty[slot]);
+                    if (GW == 2) mma_commit(&ctl->empty[(t + 1) % NU]);
+                    mma_commit(&ctl->empty[t % NU]);
+                    last_bar = &ctl->empty[t % NU];
+                    last_par = (uint32_t)(t / NU) & 1u;
                 }
                 if (!ok) break;
-                mma_commit(&ctl->acc_full);
-                if (un.kind == 0) stamp(a, kTrGuMmaDone);
+                commit_acc(buf);
+            }
+            if (ok && ndn > 0) {
+                int buf;
+                if ((ok = acquire_buf(buf))) {
+                    const uint32_t ddn = tmem + (uint32_t)(buf * 2 * Np);
+                    for (int st = 0; st < ndn; ++st, ++s, ++t) {
+                        if (!(ok = wait_stage(1))) break;
+                        if (st == 0) unit_stamp(a, ub, 0);
+                        const uint32_t sbase = smem_u32(ring + (size_t)(t % NU) * a.unit_bytes);
+                        const int nk = (min(kDnRows, Q1 - Q0 - st * kDnRows) + 15) >> 4;  // K steps of 16 positions
+                        for (int ks = 0; ks < nk; ++ks) {
+                            const uint64_t bd = desc_sw128(sbase + kDnWBytes + ks * 32, 16, 1024);
+#pragma unroll
+                            for (int mt = 0; mt < 2; ++mt) {
+                                const uint64_t ad = desc_sw128(sbase + mt * 2 * kDnLbo + ks * 2 * 1024, kDnLbo, 1024);
+                                mma_f16(ddn + mt * Np, ad, bd, id_dn, (st > 0 || ks > 0) ? 1u : 0u);
+                            }
+                        }
+                        mma_commit(&ctl->empty[t % NU]);
+                        last_bar = &ctl->empty[t % NU];
+                        last_par = (uint32_t)(t / NU) & 1u;
+                    }
+                    if (ok) commit_acc(buf);
+                }
+            }
+            // MMAs may still be reading shared memory or writing TMEM (after
+            // an abort): wait for the last commit, which covers every earlier
+            // tcgen05 operation, before the CTA releases either.
+            if (last_bar) {
+                const uint64_t t0 = globaltimer();
+                while (!mbar_test_sleep(last_bar, last_par, 1000) && globaltimer() - t0 < a.timeout_ns) {
+                }
             }
         }
         __syncwarp();
-    } else {
+    } else if (warp < kEpiWarps) {
         // ------------------------------------------------------------ epilogue
-        const int e = tid;  // TMEM lane == tile row
+        const int e = tid;  // TMEM lane == tile row (gate/up) or output column (down)
         const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
-        for (int u = 0; u < nunits; ++u) {
-            const Unit un = unit_of(pl, c, grid, u, ns);
-            const bool ok = wait_bar(&ctl->acc_full, u & 1, ctl, a.err, kErrTimeoutAcc, 20000);
-            if (!named_bar_and(2, 128, ok)) break;
+        const uint32_t peer_full = mapa_shared(smem_u32(&ctl->xchg_full), peer);
+        const uint32_t peer_free = mapa_shared(smem_u32(&ctl->xchg_free), peer);
+        // slots hold 64 rows: the half of the tile the partner finishes
+        float *myslot = a.xchg + (size_t)blockIdx.x * Np * 64;
+        const float *peerslot = a.xchg + (size_t)(blockIdx.x ^ 1) * Np * 64;
+        const uint32_t peer_recv = mapa_shared(smem_u32(xrecv), peer);
+        const bool signal = !(a.inject == 1 && rank == 1);
+        const bool mine_half = (e >> 6) == (int)rank;  // rows this CTA finishes (warp-uniform)
+        // the down unit's ids, while the gate/up stages stream
+        emit_ids16(bits, prefix, W, Q0, Q1, dn_ids, warp, kEpiWarps);
+        if (e == 0) stamp(a, kTrEmitDn);
+        mbar_arrive(&ctl->ids_ready);
+        int ub = 0;
+        bool ok = named_bar_and(kEpiBar, 128, !ctl->abort);
+        for (int i = 0; i < ntile && ok; ++i) {
+            int r0, r1;
+            tile_rows(n, ntile, i, r0, r1);
+            const int rows = r1 - r0;
+            const bool valid = e < rows;
+            const int j = valid ? gu_ids[r0 + e] : 0;
+            // While the gate/up MMAs run: this row's per-token activity bits
+            // (bit t of word t/32), so forming h reads no global memory.
+            if (mine_half) {
+                const uint32_t *mcol = a.tok_bits + (j >> 5);
+                for (int t0 = 0; t0 < Np; t0 += 32) {
+                    uint32_t word = 0;
+                    if (!a.per_token) {
+                        word = ~0u;
+                    } else if (valid) {
+#pragma unroll 8
+                        for (int q = 0; q < 32; ++q)
+                            if (t0 + q < a.B) word |= ((__ldcg(mcol + (int64_t)(t0 + q) * W) >> (j & 31)) & 1u) << q;
+                    }
+                    tokmask[(t0 >> 5) * kTileM + e] = word;
+                }
+            }
+            const int buf = ub % nbuf;
+            ok = wait_bar(&ctl->acc_full[buf], (uint32_t)(ub / nbuf) & 1u, ctl, a, kErrTimeoutAcc, a.hint_acc);
+            if (!(ok = named_bar_and(kEpiBar, 128, ok))) break;
             tc_fence_after();
-            if (e == 0) stamp(a, un.kind == 0 ? kTrGuAcc : kTrDnAcc);
-            if (un.kind == 0) {
-                const int pos = un.tile * kTileM + e;
-                const bool valid = pos < pl.U;
-                const int j = valid ? gu_ids[u * kTileM + e] : 0;
-                const bool direct = pl.Sk == 1;
-                const uint32_t *mrow = a.tok_bits + (j >> 5);
-                float *part = a.partial + (size_t)(c + u * grid) * 2 * Np * kTileM;  // gate/up item index
+            if (e == 0) unit_stamp(a, ub, 2);
+            if (i == 0 && e == 0) stamp(a, kTrGuAcc);
+            const uint32_t acc = trow + (uint32_t)(buf * 2 * Np);
+            // 1. results for the partner's rows to this CTA's slot, once the
+            //    partner has read the previous tile's
+            if (i > 0) ok = wait_bar_cluster(&ctl->xchg_free, (uint32_t)(i - 1) & 1u, ctl, a, kErrTimeoutXchg);
+            if (!(ok = named_bar_and(kEpiBar, 128, ok))) break;
+            if (!mine_half) {
                 for (int c0 = 0; c0 < Np; c0 += 16) {
-                    float gv[16], uv[16];
-                    tmem_ld16(trow + c0, gv);
-                    tmem_ld16(trow + Np + c0, uv);
-                    if (direct) {
-                        uint32_t mw[16];
+                    float v[16];
+                    tmem_ld16(acc + c0, v);
+                    tmem_ld_wait();
+                    if (a.xdsm) {
 #pragma unroll
-                        for (int i = 0; i < 16; ++i)
-                            mw[i] = (a.per_token && valid && c0 + i < a.B) ? __ldg(mrow + (int64_t)(c0 + i) * W) : ~0u;
-                        tmem_ld_wait();
-#pragma unroll
-                        for (int i = 0; i < 16; ++i) {
-                            const int t = c0 + i;
-                            float hv = 0.0f;
-                            if (valid && t < a.B && ((mw[i] >> (j & 31)) & 1u)) hv = act_h(gv[i], uv[i], a.act);
-                            a.h16[(int64_t)t * a.fpad + pos] = __float2half_rn(hv);
-                        }
+                        for (int q = 0; q < 16; ++q) st_shared_cluster_f32(peer_recv + ((c0 + q) * 64 + (e & 63)) * 4, v[q]);
                     } else {
-                        tmem_ld_wait();
 #pragma unroll
-                        for (int i = 0; i < 16; ++i) {
-                            part[(size_t)(c0 + i) * kTileM + e] = gv[i];
-                            part[(size_t)(Np + c0 + i) * kTileM + e] = uv[i];
+                        for (int q = 0; q < 16; ++q) __stcg(myslot + (size_t)(c0 + q) * 64 + (e & 63), v[q]);
+                    }
+                }
+            }
+            if (signal) mbar_arrive_remote(peer_full);
+            // 2. the partner's results for this CTA's rows
+            ok = wait_bar_cluster(&ctl->xchg_full, (uint32_t)i & 1u, ctl, a, kErrTimeoutXchg);
+            if (!(ok = named_bar_and(kEpiBar, 128, ok))) break;
+            if (i == 0 && e == 0) stamp(a, kTrXchg);
+            // 3. h = act(gate, up) * mask for this CTA's rows -> fp16 h16[t][pos]
+            const int pos = P0 + r0 + e;
+            if (mine_half) {
+                __half *hcol = a.h16 + pos;
+                for (int c0 = 0; c0 < Np; c0 += 16) {
+                    float mine[16];
+                    tmem_ld16(acc + c0, mine);
+                    float other[16];
+                    if (a.xdsm) {
+#pragma unroll
+                        for (int q = 0; q < 16; ++q) other[q] = xrecv[(c0 + q) * 64 + (e & 63)];
+                    } else {
+#pragma unroll
+                        for (int q = 0; q < 16; ++q) other[q] = __ldcg(peerslot + (size_t)(c0 + q) * 64 + (e & 63));
+                    }
+                    const uint32_t mw = tokmask[(c0 >> 5) * kTileM + e] >> (c0 & 31);
+                    tmem_ld_wait();
+                    if (valid) {
+#pragma unroll
+                        for (int q = 0; q < 16; ++q) {
+                            const int t = c0 + q;
+                            const float g = rank ? other[q] : mine[q];
+                            const float u = rank ? mine[q] : other[q];
+                            float hv = 0.0f;
+                            if (t < a.B && ((mw >> q) & 1u)) hv = act_h(g, u, a.act);
+                            hcol[(int64_t)t * a.fpad] = __float2half_rn(hv);
                         }
                     }
                 }
-                tc_fence_before();
-                mbar_arrive(&ctl->acc_empty);
-                bool writer = direct;
-                if (!direct) {
-                    __threadfence();
-                    named_bar(2, 128);
-                    if (e == 0) ctl->is_last = atomicAdd(&a.tile_cnt[un.tile], 1u) == (uint32_t)(pl.Sk - 1);
-                    named_bar(2, 128);
-                    writer = ctl->is_last != 0;
-                    if (writer) {
-                        __threadfence();
-                        for (int c0 = 0; c0 < Np; c0 += 16) {
-                            float g[16], uu[16];
-                            uint32_t mw[16];
-#pragma unroll
-                            for (int i = 0; i < 16; ++i) {
-                                g[i] = uu[i] = 0.0f;
-                                mw[i] = (a.per_token && valid && c0 + i < a.B) ? __ldg(mrow + (int64_t)(c0 + i) * W)
-                                                                              : ~0u;
-                            }
-                            for (int ks = 0; ks < pl.Sk; ++ks) {  // fixed order: deterministic sums
-                                const float *pp = a.partial + (size_t)(un.tile * pl.Sk + ks) * 2 * Np * kTileM;
-                                float pg[16], pu[16];
-#pragma unroll
-                                for (int i = 0; i < 16; ++i) {
-                                    pg[i] = __ldcg(pp + (size_t)(c0 + i) * kTileM + e);
-                                    pu[i] = __ldcg(pp + (size_t)(Np + c0 + i) * kTileM + e);
-                                }
-#pragma unroll
-                                for (int i = 0; i < 16; ++i) {
-                                    g[i] += pg[i];
-                                    uu[i] += pu[i];
-                                }
-                            }
-#pragma unroll
-                            for (int i = 0; i < 16; ++i) {
-                                const int t = c0 + i;
-                                float hv = 0.0f;
-                                if (valid && t < a.B && ((mw[i] >> (j & 31)) & 1u)) hv = act_h(g[i], uu[i], a.act);
-                                a.h16[(int64_t)t * a.fpad + pos] = __float2half_rn(hv);
-                            }
-                        }
-                    }
+                if (valid) a.merge_out[pos] = j;
+            }
+            mbar_arrive_remote(peer_free);  // the partner's slot has been read
+            tc_fence_before();
+            mbar_arrive(&ctl->acc_empty[buf]);
+            // positions [U, U rounded up to 64) of h are read by the last
+            // down stage: the cluster holding position U - 1 zeroes them
+            if (i == ntile - 1 && P0 + n == U && rank == 0) {
+                const int tail = ((U + 63) & ~63) - U;
+                for (int q = e; q < tail * Np; q += 128)
+                    a.h16[(int64_t)(q / tail) * a.fpad + U + q % tail] = __float2half_rn(0.0f);
+            }
+            // publish: h rows of this tile (and the zero tail) visible GPU-wide
+            // before the cluster's counter moves
+            __threadfence();
+            named_bar(kEpiBar, 128);
+            if (e == 0) {
+                asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.ready + clu) : "memory");
+                unit_stamp(a, ub, 3);
+            }
+            ++ub;
+        }
+        if (e == 0) stamp(a, kTrHDone);
+        if (ok && ndn > 0) {
+            // 4. the down unit: out[t][256 m + col] += acc
+            const int buf = ub % nbuf;
+            ok = wait_bar(&ctl->acc_full[buf], (uint32_t)(ub / nbuf) & 1u, ctl, a, kErrTimeoutAcc, a.hint_acc);
+            if ((ok = named_bar_and(kEpiBar, 128, ok))) {
+                tc_fence_after();
+                if (e == 0) {
+                    unit_stamp(a, ub, 2);
+                    stamp(a, kTrDnAcc);
                 }
-                if (writer) {
-                    if (valid) a.merge_out[pos] = j;
-                    __threadfence();
-                    named_bar(2, 128);
-                    if (e == 0) st_release_u32(a.tile_ready + un.tile, 1u);
-                }
-                if (e == 0) stamp(a, kTrGuPublished);
-            } else {
-#pragma unroll
-                for (int mt2 = 0; mt2 < 2; ++mt2) {
-                    const int m = un.mt * kDnCols + mt2 * kTileM + e;
-                    for (int c0 = 0; c0 < Np; c0 += 16) {
+                const uint32_t dacc = trow + (uint32_t)(buf * 2 * Np);
+#pragma unroll 1
+                for (int mt = 0; mt < 2; ++mt) {
+                    // lane 4q + r adds columns [4q, 4q + 4) of its quad for
+                    // token c0 + 4g + r: one 16-byte reduction instead of four
+                    float *oquad = a.out + m * kSlice + mt * kTileM + (e & ~3);
+                    for (int c0 = 0; c0 < Np && c0 < a.B; c0 += 16) {
                         float v[16];
-                        tmem_ld16(trow + mt2 * Np + c0, v);
+                        tmem_ld16(dacc + mt * Np + c0, v);
                         tmem_ld_wait();
 #pragma unroll
-                        for (int i = 0; i < 16; ++i)
-                            if (c0 + i < a.B) atomicAdd(a.out + (int64_t)(c0 + i) * a.d + m, v[i]);
+                        for (int g = 0; g < 4; ++g) {
+                            quad_transpose(v[4 * g], v[4 * g + 1], v[4 * g + 2], v[4 * g + 3]);
+                            const int t = c0 + 4 * g + (e & 3);
+                            if (t < a.B && a.inject != 2)
+                                red_add_v4(oquad + (int64_t)t * a.d, v[4 * g], v[4 * g + 1], v[4 * g + 2], v[4 * g + 3]);
+                        }
                     }
                 }
                 tc_fence_before();
-                mbar_arrive(&ctl->acc_empty);
+                mbar_arrive(&ctl->acc_empty[buf]);
+                if (e == 0) unit_stamp(a, ub, 3);
             }
         }
     }
 
     __syncthreads();
     if (tid == 0) stamp(a, kTrEnd);
+    // The partner may still signal this CTA's barriers until it is done.
+    cluster_sync_all();
     if (warp == kMmaWarp) {
-        if (ctl->abort) __nanosleep(100000);  // let in-flight MMAs and copies drain before freeing TMEM
         tc_fence_after();
-        tmem_dealloc(tmem, ncols);
+        tmem_dealloc(tmem, kTmemCols);
     }
 }
 
@@ -640,117 +869,185 @@ int tensor_map(const void *ptr, uint64_t cols, uint64_t rows, uint32_t box_rows,
     const cuuint64_t strides[1] = {cols * 2};
     const cuuint32_t box[2] = {64, box_rows};
     const cuuint32_t estr[2] = {1, 1};
-    CUtensorMap m;
-    memset(&m, 0, sizeof(m));
-    const CUresult r = encode(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(ptr), dims, strides, box,
+    CUtensorMap mp;
+    memset(&mp, 0, sizeof(mp));
+    const CUresult r = encode(&mp, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(ptr), dims, strides, box,
                               estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(SPB_ERR_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
     if (cache.size() > 4096) cache.clear();
-    cache.push_back({key, m});
-    *out = m;
+    cache.push_back({key, mp});
+    *out = mp;
     return SPB_OK;
 }
 
 }  // namespace
 
-// Stage geometry: K blocks per gate/up stage, neurons per down stage and ring
-// depth; both kinds of stage share the ring slots.
+// Ring geometry: K blocks per gate/up stage, unit size and unit count.  A
+// down stage (64 W_down rows x 256 columns + the h tile) fills one unit; a
+// gate/up stage (nkb K blocks of 128 rows + the activation tile) one or two.
 struct Geometry {
-    int nkb, ns, P;
-    uint32_t stage_bytes;
+    int nkb, nu, gw;
+    uint32_t unit_bytes;
     size_t smem;
 };
 
-static Geometry pick_geometry(int Np, int W, int max_chunk, int d) {
-    const size_t fixed = sizeof(TcCtl) + sizeof(int) * (kMaxGuUnits * kTileM + max_chunk) + 1024 + 64;
-    const size_t prologue = sizeof(int) * (W + 1 + 64) + sizeof(uint32_t) * W;  // in the ring
+// Pairs exchange their gate/up halves through distributed shared memory up
+// to this batch width (an [Np][64] fp32 receive buffer), through L2 above it.
+constexpr int kXdsmMaxNp = 64;
+
+static size_t fixed_smem(int Np, int W, int max_gu, int max_dn) {
+    return sizeof(TcCtl) + sizeof(uint32_t) * 8 * kTileM + sizeof(uint16_t) * (size_t)(max_gu + max_dn) + 16 +
+           (Np <= kXdsmMaxNp ? sizeof(float) * 64 * (size_t)Np : 0) + sizeof(int) * (size_t)(2 * W + 65) + 1024 + 64;
+}
+
+static Geometry pick_geometry(int Np, int W, int max_gu, int max_dn, int d, int force_nkb, int force_units) {
+    const size_t fixed = fixed_smem(Np, W, max_gu, max_dn);
     const size_t budget = 227 * 1024;
-    const char *env = getenv("SPB_TC_NKB");
-    const int forced = env ? atoi(env) : 0;
-    // The producer warps' copy rate follows the weight bytes in flight: maximise (P - 1) x the smaller of the gate/up and down
-    // stages' weight bytes; prefer longer row runs on ties.
+    const uint32_t dn = (kDnWBytes + (uint32_t)Np * 128 + 1023) & ~1023u;
+    // The copy rate follows the weight bytes in flight and the contiguous run
+    // per row (128 * nkb bytes): score the smaller of the gate/up and down
+    // weight bytes in flight, weighted towards longer runs.
     Geometry best{0, 0, 0, 0, 0};
     size_t best_score = 0;
-    for (int nkb = 4; nkb >= 1; --nkb) {
-        if (forced && nkb != forced) continue;
+    for (int nkb = 4; nkb >= 1; nkb >>= 1) {
+        if (force_nkb && nkb != force_nkb) continue;
         if ((d / 64) % nkb) continue;
-        for (int ns = 128; ns >= 64; ns -= 64) {
-            const uint32_t gu = (uint32_t)nkb * (2 * kATile + (uint32_t)Np * 128);
-            const uint32_t dn = (uint32_t)ns * 512 + (uint32_t)(ns / 64) * Np * 128;
-            const uint32_t stage = ((gu > dn ? gu : dn) + 1023) & ~1023u;
-            if (fixed + 2 * (size_t)stage > budget || 2 * (size_t)stage < prologue) continue;
-            const int P = (int)std::min<size_t>((budget - fixed) / stage, kMaxStages);
-            const size_t w_gu = (size_t)nkb * 2 * kATile, w_dn = (size_t)ns * 512;
-            // rank: the longer row run, then the weight bytes in flight
-            const size_t score = ((size_t)nkb << 40) + (size_t)(P - 1) * std::min(w_gu, w_dn);
-            if (score > best_score) {
-                best_score = score;
-                best = Geometry{nkb, ns, P, stage, fixed + (size_t)P * stage};
-            }
+        const uint32_t gu = ((uint32_t)nkb * (kATile + (uint32_t)Np * 128) + 1023) & ~1023u;
+        uint32_t unit = dn > (gu + 1) / 2 ? dn : (((gu + 1) / 2 + 1023) & ~1023u);
+        const int gw = gu > unit ? 2 : 1;
+        if (gw == 1) unit = gu > dn ? gu : dn;
+        if (budget < fixed + 2u * gw * unit) continue;
+        int nu = (int)std::min<size_t>((budget - fixed) / unit, kMaxUnits);
+        if (force_units) nu = std::min(nu, force_units);
+        if (gw == 2) nu &= ~1;
+        if (nu < 2 * gw) continue;
+        const size_t in_gu = (size_t)(nu / gw - 1) * nkb * kATile, in_dn = (size_t)(nu - 1) * kDnWBytes;
+        const size_t score = std::min(in_gu, in_dn) * (size_t)(nkb * nkb);
+        if (score > best_score) {
+            best_score = score;
+            best = Geometry{nkb, nu, gw, unit, fixed + (size_t)nu * unit};
         }
     }
     return best;
 }
 
+// Clusters of two that can be resident at once with `smem` bytes per CTA
+// (cached per device and size).
+static int max_clusters(size_t smem, int sms) {
+    static std::mutex mu;
+    static std::vector<std::pair<std::pair<int, size_t>, int>> cache;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return sms / 2;
+    std::lock_guard<std::mutex> lk(mu);
+    for (auto &e : cache)
+        if (e.first.first == dev && e.first.second == smem) return e.second;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * (sms / 2));
+    cfg.blockDim = dim3(kTcThreads);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, (const void *)ffn_tc_kernel, &cfg) != cudaSuccess || n <= 0) {
+        cudaGetLastError();
+        n = sms / 2;
+    }
+    n = std::min(n, sms / 2);
+    cache.push_back({{dev, smem}, n});
+    return n;
+}
+
 int launch_ffn_tc(const TcLaunch &L, cudaStream_t st) {
     const int Np = L.Np;
     if (Np < 16 || Np > 256 || Np % 16) return fail(SPB_ERR_UNSUPPORTED, "tensor path: batch must be 1..256");
-    if (L.d % kDnCols) return fail(SPB_ERR_INVALID, "tensor path: d must be a multiple of 256");
+    if (L.d % kSlice) return fail(SPB_ERR_INVALID, "tensor path: d must be a multiple of 256");
+    const DebugHooks &dbg = debug_hooks();
     TcArgs a{};
     a.wg = static_cast<const __half *>(L.wg);
     a.wu = static_cast<const __half *>(L.wu);
     a.wd = static_cast<const __half *>(L.wd);
+    a.labels = L.labels;
+    a.tok_in = L.tok_in;
+    a.x = L.x;
+    a.x16 = L.x16;
+    a.gbar = L.gbar;
     a.h16 = L.h16;
     a.seg_bits = L.seg_bits;
     a.tok_bits = L.tok_bits;
     a.out = L.out;
     a.merge_out = L.merge_out;
     a.count_out = L.count_out;
-    a.partial = L.partial;
-    a.tile_cnt = L.tile_cnt;
-    a.tile_ready = L.tile_ready;
+    a.xchg = L.xchg;
+    a.ready = L.ready;
     a.err = L.err;
     a.trace = static_cast<unsigned long long *>(trace_buffer((size_t)kStageTraceBase + kStageTraceMax * 4));
     a.B = L.B;
     a.Np = Np;
     a.d = L.d;
     a.f = L.f;
-    a.fpad = L.fpad;
     a.W = words_of(L.f);
+    a.fpad = L.fpad;
     a.act = L.act;
     a.per_token = L.per_token;
-    a.debug = getenv("SPB_TC_DEBUG") ? atoi(getenv("SPB_TC_DEBUG")) : 0;
-    a.force_sk = getenv("SPB_TC_SK") ? atoi(getenv("SPB_TC_SK")) : 0;
-    // Longest down chunk: ceil(T / KC) tiles with KC = min(T, grid / MT).
-    const int Tmax = (L.f + kTileM - 1) / kTileM;
-    const int MT = L.d / kDnCols;
-    const int KCmin = std::max(1, std::min(Tmax, L.grid / MT));
-    const int max_chunk = ((Tmax + KCmin - 1) / KCmin + 1) * kTileM;
-    if ((Tmax + L.grid - 1) / L.grid > kMaxGuUnits) return fail(SPB_ERR_UNSUPPORTED, "tensor path: f too large");
-    const Geometry g = pick_geometry(Np, a.W, max_chunk, L.d);
-    if (g.P < 2) return fail(SPB_ERR_UNSUPPORTED, "tensor path: shared memory too small for two stages");
-    a.P = g.P;
+    a.timeout_ns = dbg.timeout_ns ? dbg.timeout_ns : kDefaultTimeoutNs;
+    a.hint_acc = dbg.hint_acc ? dbg.hint_acc : 20000;
+    a.hint = dbg.hint ? dbg.hint : 1000;
+    a.inject = dbg.inject;
+    a.nbuf = std::min<int>(kMaxBufs, (int)kTmemCols / (2 * Np));
+    a.xdsm = Np <= kXdsmMaxNp ? 1 : 0;
+
+    const int sms = std::min(L.grid, kMaxTcGrid);
+    const int MT = L.d / kSlice;
+    // size the id tables for the most clusters this device can hold, then
+    // check the launch against the real count
+    int nclu = sms / 2;
+    Geometry g{};
+    int rc;
+    for (int pass = 0; pass < 2; ++pass) {
+        a.KC = std::max(1, (2 * nclu) / MT);
+        a.max_gu = (L.f + nclu - 1) / nclu + 1;
+        a.max_dn = (L.f + a.KC - 1) / a.KC + 128;
+        g = pick_geometry(Np, a.W, a.max_gu, a.max_dn, L.d, dbg.nkb, dbg.stages);
+        if (g.nu < 2) return fail(SPB_ERR_UNSUPPORTED, "tensor path: shared memory too small for two stages");
+        if ((rc = ensure_smem((const void *)ffn_tc_kernel, g.smem))) return rc;
+        const int fit = max_clusters(g.smem, sms);
+        if (fit >= nclu) break;
+        nclu = std::max(1, fit);
+    }
+    a.nu = g.nu;
+    a.gw = g.gw;
     a.nkb = g.nkb;
-    a.ns = g.ns;
-    a.stage_bytes = g.stage_bytes;
+    a.unit_bytes = g.unit_bytes;
 
     TcMaps maps;
-    int rc;
     if ((rc = tensor_map(L.x16, L.d, Np, Np, &maps.x))) return rc;
     if ((rc = tensor_map(L.h16, L.fpad, Np, Np, &maps.h))) return rc;
-    if ((rc = ensure_smem((const void *)ffn_tc_kernel, g.smem))) return rc;
 
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(L.grid);
+    cfg.gridDim = dim3(2 * nclu);
     cfg.blockDim = dim3(kTcThreads);
     cfg.dynamicSmemBytes = g.smem;
     cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchAttribute attr[3];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    // CTAs of the down phase wait for h that CTAs of other clusters publish:
+    // the cooperative launch guarantees every CTA is resident at once (the
+    // launch fails instead if the grid cannot be)
+    attr[1].id = cudaLaunchAttributeCooperative;
+    attr[1].val.cooperative = 1;
+    attr[2].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[2].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 3;
     SPB_CUDA_TRY(cudaLaunchKernelEx(&cfg, ffn_tc_kernel, maps, a));
     return SPB_OK;
 }

@@ -156,6 +156,10 @@ __device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t *p) {
     return v;
 }
 
+__device__ __forceinline__ void red_add_release_u32(uint32_t *p, uint32_t v) {
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
 __device__ __forceinline__ void st_release_u32(uint32_t *p, uint32_t v) {
     asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
@@ -169,6 +173,93 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void *tmap, uint
         " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
         "l"(reinterpret_cast<uint64_t>(tmap)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
         : "memory");
+}
+
+
+// ---- thread-block clusters ------------------------------------------------------
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+// Address of the same shared-memory location in cluster CTA `rank`.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+    return r;
+}
+
+// Arrive on an mbarrier of another CTA of the cluster (address from
+// mapa_shared); release at cluster scope orders this thread's earlier global
+// and shared stores before the arrival.
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+// mbar_test_sleep with acquire at cluster scope: after it succeeds, stores
+// that a partner CTA made before its releasing arrival are visible.
+__device__ __forceinline__ bool mbar_test_cluster(uint64_t *bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+
+// 4-byte store into another CTA's shared memory (address from mapa_shared).
+__device__ __forceinline__ void st_shared_cluster_f32(uint32_t cluster_addr, float v) {
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(cluster_addr), "f"(v) : "memory");
+}
+
+// Every thread of every CTA of the cluster.
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+__device__ __forceinline__ void grid_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Four consecutive fp32 values added to global memory in one reduction
+// (16-byte aligned address).
+__device__ __forceinline__ void red_add_v4(float *p, float a, float b, float c, float d) {
+    asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d)
+                 : "memory");
+}
+
+// 4 x 4 transpose across each quad of lanes: lane 4q + r holds row r
+// (x0..x3) on entry and column r of the quad's matrix on return.
+__device__ __forceinline__ void quad_transpose(float &x0, float &x1, float &x2, float &x3) {
+    const int lane = threadIdx.x & 31;
+    bool hi = (lane & 2) != 0;
+    float s0 = hi ? x0 : x2, s1 = hi ? x1 : x3;
+    float r0 = __shfl_xor_sync(0xffffffffu, s0, 2), r1 = __shfl_xor_sync(0xffffffffu, s1, 2);
+    if (hi) {
+        x0 = r0;
+        x1 = r1;
+    } else {
+        x2 = r0;
+        x3 = r1;
+    }
+    hi = (lane & 1) != 0;
+    s0 = hi ? x0 : x1;
+    s1 = hi ? x2 : x3;
+    r0 = __shfl_xor_sync(0xffffffffu, s0, 1);
+    r1 = __shfl_xor_sync(0xffffffffu, s1, 1);
+    if (hi) {
+        x0 = r0;
+        x2 = r1;
+    } else {
+        x1 = r0;
+        x3 = r1;
+    }
 }
 
 // ---- programmatic dependent launch -------------------------------------------

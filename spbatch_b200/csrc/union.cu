@@ -29,8 +29,12 @@ constexpr int kUnionWarps = 8;
 __global__ void __launch_bounds__(kUnionWarps * 32)
 union_bits_kernel(const float *__restrict__ idx, int B, int f, int W, int G, uint32_t *__restrict__ tok_bits,
                   uint32_t *__restrict__ seg_bits, PrepJobs jobs) {
-    // Let a dependent launch (programmatic dependent launch) start its
-    // prologue now; it still waits for this grid's results before reading them.
+    // Launched with programmatic dependent launch: the CTAs may be resident
+    // before the previous kernel on the stream finishes, and wait here until
+    // its results are visible.  The dependent launch (the FFN kernel) may
+    // then start its prologue; it waits for this grid's results before
+    // reading them.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int lane = threadIdx.x & 31;
     const int w = blockIdx.x * kUnionWarps + (threadIdx.x >> 5);
@@ -138,8 +142,16 @@ int launch_union_bits(const float *idx, int B, int f, int G, uint32_t *tok_bits,
     const int W = words_of(f);
     int grid = (W + kUnionWarps - 1) / kUnionWarps;
     if (jobs.x16 || jobs.zero_out) grid = max(grid, num_sms());
-    union_bits_kernel<<<grid, kUnionWarps * 32, 0, st>>>(idx, B, f, W, G, tok_bits, seg_bits, jobs);
-    SPB_LAUNCH_CHECK("union_bits_kernel");
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kUnionWarps * 32);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    SPB_CUDA_TRY(cudaLaunchKernelEx(&cfg, union_bits_kernel, idx, B, f, W, G, tok_bits, seg_bits, jobs));
     return SPB_OK;
 }
 

@@ -84,3 +84,30 @@ def test_library_quantizer_matches_oracle(spb, oracle_mod):
     for qt, code in ((8, spb.W_Q8_0), (4, spb.W_Q4_0)):
         np.testing.assert_array_equal(spb.quantize(w, code), oracle_mod.quantize(w, qt))
         assert spb.lib().spb_weight_row_bytes(code, 4096) == (4096 if qt == 8 else 2048) + 256
+
+
+def test_product_library_has_no_debug_hooks(spb):
+    """The failure-injection hooks exist only in the test-hook build."""
+    assert not hasattr(spb.lib(), "spb_debug_config")
+    names = _declared("spb_debug.h", r"\b(spb_[a-z0-9_]+)\s*\(")
+    assert names == ["spb_debug_config"]
+    for n in names:
+        assert hasattr(spb.debug_lib(), n)
+
+
+def test_tensor_path_rejects_before_launch(spb):
+    """Requests the tensor path cannot serve fail on the host, before any launch."""
+    L = spb.lib()
+    fake = C.c_void_p(256)
+    # f above 32768 neurons (1024 bit words of union)
+    rc = L.spb_ffn_forward(fake, fake, fake, 0, fake, fake, 8, 4096, 32769, 0, 1, 2, fake, None, None, fake,
+                           1 << 40, None)
+    assert rc == 4 and b"f > 32768" in L.spb_last_error()
+    # d not a multiple of 256
+    rc = L.spb_ffn_forward(fake, fake, fake, 0, fake, fake, 8, 384, 1024, 0, 1, 2, fake, None, None, fake,
+                           1 << 40, None)
+    assert rc == 1 and b"d % 256" in L.spb_last_error()
+    # quantised weights on the tensor path
+    rc = L.spb_ffn_forward(fake, fake, fake, 1, fake, fake, 8, 4096, 1024, 0, 1, 2, fake, None, None, fake,
+                           1 << 40, None)
+    assert rc == 4 and b"fp16" in L.spb_last_error()

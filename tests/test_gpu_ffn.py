@@ -4,7 +4,7 @@ indices bit-exact)."""
 import numpy as np
 import pytest
 
-from conftest import assert_close
+from conftest import assert_close, assert_close_70b
 from spbatch_b200.workload import zipf_active_labels
 
 pytestmark = pytest.mark.gpu
@@ -226,3 +226,114 @@ def test_stream_path_many_calls(spb, cuda, oracle_mod):
     for x, l, o in zip(xs, labs, outs):
         assert_close(o.cpu().numpy(), oracle_mod.ffn(wg, wu, wd, x, l))
     assert _ws_error(ws) == 0
+
+
+def _gpu_layer(cuda, d, f, seed, std=0.02):
+    """fp16 N(0, std^2) weights drawn on the GPU (fast at 70B size), with host copies for the oracle."""
+    import torch
+    g = torch.Generator(device=cuda)
+    g.manual_seed(seed)
+    Wd = [(torch.randn((f, d), generator=g, device=cuda) * std).half() for _ in range(3)]
+    return Wd, [w.cpu().numpy() for w in Wd]
+
+
+def _tensor_case(spb, cuda, oracle_mod, d, f, B, k, seed, check_tokens, lab=None):
+    """Tensor path on (d, f, B) with Zipf activity: union bit-exact, the output
+    rows of `check_tokens` against the oracle (with the per-token mask a token's
+    output depends only on its own active set, so the oracle runs on those
+    tokens alone)."""
+    import torch
+    Wd, Wh = _gpu_layer(cuda, d, f, seed)
+    x = np.random.default_rng(seed).standard_normal((B, d)).astype(np.float32)
+    if lab is None:
+        lab = zipf_active_labels(B, f, k, seed=seed)
+    ws = spb.new_workspace(B, d, f, 0, cuda)
+    merge = torch.full((f,), -1, dtype=torch.int32, device=cuda)
+    count = torch.zeros(1, dtype=torch.int32, device=cuda)
+    out = spb.ffn_forward(*Wd, _dev(x, cuda), _dev(lab, cuda), merge_idx_out=merge, count_out=count,
+                          workspace=ws, path=spb.PATH_TENSOR)
+    torch.cuda.synchronize()
+    assert _ws_error(ws) == 0
+    ref_idx = np.nonzero((lab > 0).any(0))[0]
+    U = int(count.cpu()[0])
+    assert U == len(ref_idx)
+    np.testing.assert_array_equal(merge.cpu().numpy()[:U], ref_idx)
+    tok = np.asarray(check_tokens)
+    (assert_close_70b if d >= 8192 else assert_close)(out.cpu().numpy()[tok], oracle_mod.ffn(*Wh, x[tok], lab[tok]))
+    return U
+
+
+@pytest.mark.parametrize("B", [16, 32])
+def test_tensor_path_70b_zipf(spb, cuda, oracle_mod, B):
+    """Config 5 layer (d=8192, f=28672), 10% Zipf activity: the union spans
+    ~150-190 tiles, so every cluster walks two or three tiles."""
+    U = _tensor_case(spb, cuda, oracle_mod, 8192, 28672, B, 2867, 70 + B, [0, B // 2 + 1, B - 1])
+    assert U > 74 * 128  # more than one tile per cluster of two SMs
+
+
+def test_tensor_path_70b_b256(spb, cuda, oracle_mod):
+    """Largest config-5 batch: N = 256 (the MMA's widest tile), union dense."""
+    U = _tensor_case(spb, cuda, oracle_mod, 8192, 28672, 256, 2867, 256, [0, 129, 255])
+    assert U == 28672
+
+
+@pytest.mark.parametrize("B", [128, 200, 256])
+def test_tensor_path_wide_batches(spb, cuda, oracle_mod, B):
+    """N = 128 / 208 / 256 at a small layer with a fully dense union."""
+    lab = np.ones((B, 4096), np.float32)
+    _tensor_case(spb, cuda, oracle_mod, 1024, 4096, B, 0, 500 + B, [0, B // 3, B - 1], lab=lab)
+
+
+def test_tensor_path_7b_b64_b128(spb, cuda, oracle_mod):
+    for B in (64, 128):
+        _tensor_case(spb, cuda, oracle_mod, 4096, 11008, B, 1101, 640 + B, [0, B - 1])
+
+
+def test_tensor_path_tiny_union(spb, cuda, oracle_mod):
+    """Fewer active neurons than clusters: most clusters own nothing."""
+    B, f = 8, 4096
+    lab = np.zeros((B, f), np.float32)
+    lab[:, [3, 700, 701, 4000, 4095]] = 1.0
+    lab[5, 9] = 1.0
+    _tensor_case(spb, cuda, oracle_mod, 512, f, B, 0, 77, list(range(B)), lab=lab)
+
+
+@pytest.mark.parametrize("B", [5, 6, 7])
+@pytest.mark.parametrize("wtype", [1, 2])
+def test_quantised_token_groups_ragged(spb, cuda, oracle_mod, B, wtype):
+    """Quantised batches above the streaming kernel's 4 tokens run as one
+    launch per token group; ragged last group (B % 4 != 0, B = 5 leaves a
+    one-token group) and ragged f, all launches sharing one workspace."""
+    import torch
+    rng = np.random.default_rng(900 + B + wtype)
+    d, f = 1024, 2050
+    Wf = [(rng.standard_normal((f, d)) * 0.02).astype(np.float32) for _ in range(3)]
+    qt = 8 if wtype == 1 else 4
+    Q = [spb.quantize(w, wtype) for w in Wf]
+    Wdq = [oracle_mod.dequantize(q, qt, d) for q in Q]
+    x = rng.standard_normal((B, d)).astype(np.float32)
+    lab = zipf_active_labels(B, f, 205, seed=B)
+    ws = spb.new_workspace(B, d, f, 0, cuda)
+    out = spb.ffn_forward(*[_dev(q, cuda) for q in Q], _dev(x, cuda), _dev(lab, cuda), wtype=wtype, workspace=ws,
+                          path=spb.PATH_GEMV)
+    torch.cuda.synchronize()
+    assert _ws_error(ws) == 0
+    assert_close(out.cpu().numpy(), oracle_mod.ffn_f32w(*Wdq, x, lab))
+
+
+@pytest.mark.parametrize("B", [3, 4])
+def test_gemv_70b_token_groups(spb, cuda, oracle_mod, B):
+    """fp16 d=8192 with B > 2 runs as two-token streaming launches (a ragged
+    one-token tail at B = 3); ragged f."""
+    import torch
+    rng = np.random.default_rng(950 + B)
+    d, f = 8192, 3001
+    W = _layer(rng, d, f)
+    x = rng.standard_normal((B, d)).astype(np.float32)
+    lab = zipf_active_labels(B, f, 300, seed=B)
+    ws = spb.new_workspace(B, d, f, 0, cuda)
+    out = spb.ffn_forward(*[_dev(w, cuda) for w in W], _dev(x, cuda), _dev(lab, cuda), workspace=ws,
+                          path=spb.PATH_GEMV)
+    torch.cuda.synchronize()
+    assert _ws_error(ws) == 0
+    assert_close(out.cpu().numpy(), oracle_mod.ffn(*W, x, lab))
