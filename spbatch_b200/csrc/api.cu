@@ -286,6 +286,7 @@ int spb_debug_config(int key, long long value) {
         case SPB_DEBUG_TC_STAGES: g_debug.stages = (int)value; return SPB_OK;
         case SPB_DEBUG_TC_HINT_ACC: g_debug.hint_acc = (uint32_t)value; return SPB_OK;
         case SPB_DEBUG_TC_HINT: g_debug.hint = (uint32_t)value; return SPB_OK;
+        case SPB_DEBUG_TC_SPLIT_STAGES: g_debug.split_stages = (int)value; return SPB_OK;
         default: return fail(SPB_ERR_INVALID, "spb_debug_config: unknown key");
     }
 }

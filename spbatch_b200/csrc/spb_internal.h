@@ -103,6 +103,7 @@ struct DebugHooks {
     int stages = 0;           // tensor path: cap the ring depth
     uint32_t hint_acc = 0;    // tensor path: suspend hint of the epilogue's accumulator waits (ns)
     uint32_t hint = 0;        // tensor path: suspend hint of the ring waits (ns)
+    int split_stages = 0;     // tensor path: split gate/up stages over two ring units
 };
 const DebugHooks &debug_hooks();
 

@@ -109,7 +109,6 @@ struct TcArgs {
     __half *x16;                 // [Np][d] fp16 activations (rows >= B zero), written in phase 0
     __half *h16;                 // [Np][fpad] h, K-major per token
     uint32_t *seg_bits;          // [W] batch union, written in phase 0
-    uint32_t *tok_bits;          // [B][W] per-token bits, written in phase 0
     unsigned int *gbar;          // [2] grid barrier: arrival count, generation
     float *out;                  // [B][d], zero on entry
     int32_t *merge_out;          // [f]
@@ -355,25 +354,20 @@ ffn_tc_kernel(const __grid_constant__ TcMaps maps, const TcArgs a) {
             const bool in = j < a.f;
             uint32_t seg = 0;
             if (a.tok_in) {
-                for (int t = lane; t < a.B; t += 32) {
-                    const uint32_t b = a.tok_in[(int64_t)t * W + w] & (w == W - 1 && (a.f & 31) ? (1u << (a.f & 31)) - 1u : ~0u);
-                    a.tok_bits[(int64_t)t * W + w] = b;
-                    seg |= b;
-                }
-                seg = __reduce_or_sync(0xffffffffu, seg);
+                for (int t = lane; t < a.B; t += 32) seg |= __ldg(a.tok_in + (int64_t)t * W + w);
+                seg = __reduce_or_sync(0xffffffffu, seg) & (w == W - 1 && (a.f & 31) ? (1u << (a.f & 31)) - 1u : ~0u);
             } else {
+                // lane j: is neuron 32 w + j active for any token (all of a
+                // 32-token group's labels in flight at once)
+                bool any = false;
                 for (int t0 = 0; t0 < a.B; t0 += 32) {
-                    // every token of a 32-token group in flight at once
                     float v[32];
 #pragma unroll
                     for (int q = 0; q < 32; ++q) v[q] = (in && t0 + q < a.B) ? __ldg(a.labels + (int64_t)(t0 + q) * a.f + j) : 0.0f;
 #pragma unroll
-                    for (int q = 0; q < 32; ++q) {
-                        const uint32_t b = __ballot_sync(0xffffffffu, v[q] > 0.0f);
-                        if (lane == q && t0 + q < a.B) a.tok_bits[(int64_t)(t0 + q) * W + w] = b;
-                        seg |= b;
-                    }
+                    for (int q = 0; q < 32; ++q) any |= v[q] > 0.0f;
                 }
+                seg = __ballot_sync(0xffffffffu, any);
             }
             if (lane == 0) a.seg_bits[w] = seg;
         }
@@ -684,15 +678,20 @@ ffn_tc_kernel(const __grid_constant__ TcMaps maps, const TcArgs a) {
             // While the gate/up MMAs run: this row's per-token activity bits
             // (bit t of word t/32), so forming h reads no global memory.
             if (mine_half) {
-                const uint32_t *mcol = a.tok_bits + (j >> 5);
                 for (int t0 = 0; t0 < Np; t0 += 32) {
                     uint32_t word = 0;
                     if (!a.per_token) {
                         word = ~0u;
-                    } else if (valid) {
+                    } else if (valid && a.tok_in) {
+                        const uint32_t *mcol = a.tok_in + (j >> 5);
 #pragma unroll 8
                         for (int q = 0; q < 32; ++q)
-                            if (t0 + q < a.B) word |= ((__ldcg(mcol + (int64_t)(t0 + q) * W) >> (j & 31)) & 1u) << q;
+                            if (t0 + q < a.B) word |= ((__ldg(mcol + (int64_t)(t0 + q) * W) >> (j & 31)) & 1u) << q;
+                    } else if (valid) {
+                        const float *lcol = a.labels + j;
+#pragma unroll 8
+                        for (int q = 0; q < 32; ++q)
+                            if (t0 + q < a.B) word |= (__ldg(lcol + (int64_t)(t0 + q) * a.f) > 0.0f ? 1u : 0u) << q;
                     }
                     tokmask[(t0 >> 5) * kTileM + e] = word;
                 }
@@ -901,7 +900,8 @@ static size_t fixed_smem(int Np, int W, int max_gu, int max_dn) {
            (Np <= kXdsmMaxNp ? sizeof(float) * 64 * (size_t)Np : 0) + sizeof(int) * (size_t)(2 * W + 65) + 1024 + 64;
 }
 
-static Geometry pick_geometry(int Np, int W, int max_gu, int max_dn, int d, int force_nkb, int force_units) {
+static Geometry pick_geometry(int Np, int W, int max_gu, int max_dn, int d, int force_nkb, int force_units,
+                              bool split_stages) {
     const size_t fixed = fixed_smem(Np, W, max_gu, max_dn);
     const size_t budget = 227 * 1024;
     const uint32_t dn = (kDnWBytes + (uint32_t)Np * 128 + 1023) & ~1023u;
@@ -914,7 +914,11 @@ static Geometry pick_geometry(int Np, int W, int max_gu, int max_dn, int d, int 
         if (force_nkb && nkb != force_nkb) continue;
         if ((d / 64) % nkb) continue;
         const uint32_t gu = ((uint32_t)nkb * (kATile + (uint32_t)Np * 128) + 1023) & ~1023u;
-        uint32_t unit = dn > (gu + 1) / 2 ? dn : (((gu + 1) / 2 + 1023) & ~1023u);
+        // Splitting a gate/up stage over two units lets more down stages fly,
+        // but the extra barrier waits in the MMA issue loop cost more than
+        // that gains (measured): one unit per stage unless asked otherwise.
+        uint32_t unit = gu > dn ? gu : dn;
+        if (split_stages) unit = dn > (gu + 1) / 2 ? dn : (((gu + 1) / 2 + 1023) & ~1023u);
         const int gw = gu > unit ? 2 : 1;
         if (gw == 1) unit = gu > dn ? gu : dn;
         if (budget < fixed + 2u * gw * unit) continue;
@@ -979,7 +983,6 @@ int launch_ffn_tc(const TcLaunch &L, cudaStream_t st) {
     a.gbar = L.gbar;
     a.h16 = L.h16;
     a.seg_bits = L.seg_bits;
-    a.tok_bits = L.tok_bits;
     a.out = L.out;
     a.merge_out = L.merge_out;
     a.count_out = L.count_out;
@@ -1013,7 +1016,7 @@ int launch_ffn_tc(const TcLaunch &L, cudaStream_t st) {
         a.KC = std::max(1, (2 * nclu) / MT);
         a.max_gu = (L.f + nclu - 1) / nclu + 1;
         a.max_dn = (L.f + a.KC - 1) / a.KC + 128;
-        g = pick_geometry(Np, a.W, a.max_gu, a.max_dn, L.d, dbg.nkb, dbg.stages);
+        g = pick_geometry(Np, a.W, a.max_gu, a.max_dn, L.d, dbg.nkb, dbg.stages, dbg.split_stages != 0);
         if (g.nu < 2) return fail(SPB_ERR_UNSUPPORTED, "tensor path: shared memory too small for two stages");
         if ((rc = ensure_smem((const void *)ffn_tc_kernel, g.smem))) return rc;
         const int fit = max_clusters(g.smem, sms);
