@@ -103,6 +103,24 @@ int spb_ffn_forward(const void *w_gate, const void *w_up, const void *w_down, in
                     void *stream);
 
 /*
+ * spb_ffn_forward with the active sets as per-token bit words instead of fp32
+ * labels: tok_bits [B][ceil(f/32)], bit (j % 32) of word j / 32 of row t set
+ * iff neuron j is active for token t -- the layout spb_predict writes to
+ * bits_out and spb_union to tok_bits.  Everything else, the results included,
+ * is as for spb_ffn_forward.  The per-token sets cross PCIe / HBM as 1/32 of
+ * the label bytes, and no pass over [B][f] labels precedes the layer: the
+ * tensor-core path builds the union in every CTA from these words, with no
+ * grid-wide step.  Replaces the label input of get_idx_cuda
+ * (cuda/kernel.cuh:97, cuda/kernel.cu:877-937) for callers whose predictor
+ * emits sets rather than labels (DejaVu_predictor/trainer_mlp.py:35-37 turns
+ * logits into sets).
+ */
+int spb_ffn_forward_bits(const void *w_gate, const void *w_up, const void *w_down, int wtype, const float *x,
+                         const uint32_t *tok_bits, int B, int d, int f, int act, int per_token_mask, int path,
+                         float *out, int32_t *merge_idx_out, int32_t *count_out, void *workspace,
+                         size_t workspace_bytes, void *stream);
+
+/*
  * Block-quantised weights (BASELINE: ggml Q8_0 / Q4_0; the reference has only
  * the f16 instance of its block-dequantisation hook, cuda/kernel.cuh:69,
  * cuda/kernel.cu:337-356).  Rows use the "split" layout: all quant bytes of
@@ -127,16 +145,18 @@ int spb_dequantize_rows(const void *q, int wtype, int rows, int d, float *out, v
  *   reduction order, so logits and index sets reproduce bit-for-bit)
  *   k > 0: the k largest logits per token are active (ties -> lower id);
  *   k = 0: logit >= threshold is active (threshold 0 = sigmoid >= 0.5)
- *   labels_out [B][f] fp32: 1 active / 0 inactive -- the label format
+ *   labels_out [B][f] fp32 (nullable): 1 active / 0 inactive -- the label format
  *              spb_union / spb_ffn_forward consume
+ *   bits_out   [B][ceil(f/32)] (nullable): the same sets as bit words, the
+ *              input of spb_ffn_forward_bits; labels_out or bits_out needed
  *   idx_out    [B][k > 0 ? k : f] (nullable): ascending active ids per token
  *   count_out  [B] (nullable), logits_out [B][f] (nullable)
  * d and D must be multiples of 256; workspace: spb_predict_workspace_bytes.
  */
 size_t spb_predict_workspace_bytes(int B, int D, int f);
 int spb_predict(const void *p1, const void *p2, const float *x, int B, int d, int D, int f, int k, float threshold,
-                float *labels_out, int32_t *idx_out, int32_t *count_out, float *logits_out, void *workspace,
-                size_t workspace_bytes, void *stream);
+                float *labels_out, uint32_t *bits_out, int32_t *idx_out, int32_t *count_out, float *logits_out,
+                void *workspace, size_t workspace_bytes, void *stream);
 
 /*
  * Allocation-free variant of spb_union for callers that cannot allocate

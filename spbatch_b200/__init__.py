@@ -70,7 +70,8 @@ def _bind(L: C.CDLL) -> None:
     L.spb_dequantize_rows.argtypes = [P, I, I, I, P, P]
     L.spb_predict_workspace_bytes.argtypes = [I, I, I]
     L.spb_predict_workspace_bytes.restype = Z
-    L.spb_predict.argtypes = [P, P, P, I, I, I, I, I, C.c_float, P, P, P, P, P, Z, P]
+    L.spb_predict.argtypes = [P, P, P, I, I, I, I, I, C.c_float, P, P, P, P, P, P, Z, P]
+    L.spb_ffn_forward_bits.argtypes = [P, P, P, I, P, P, I, I, I, I, I, I, P, P, P, P, Z, P]
     L.spb_ffn_forward.argtypes = [P, P, P, I, P, P, I, I, I, I, I, I, P, P, P, P, Z, P]
     L.spb_ffn_launches.argtypes = [I, I, I, I]
     L.spb_trace_enable.argtypes = [P, Z]
@@ -141,27 +142,34 @@ def union(idx, group: int = 0, workspace=None, stream=None):
     return merge, act, bits
 
 
-def ffn_forward(w_gate, w_up, w_down, x, idx, *, wtype: int = W_F16, act: int = ACT_RELU_MUL,
-                per_token_mask: bool = True, path: int = PATH_AUTO, out=None, workspace=None,
-                merge_idx_out=None, count_out=None, stream=None, check: bool = False):
+def ffn_forward(w_gate, w_up, w_down, x, idx=None, *, bits=None, f: int | None = None, wtype: int = W_F16,
+                act: int = ACT_RELU_MUL, per_token_mask: bool = True, path: int = PATH_AUTO, out=None,
+                workspace=None, merge_idx_out=None, count_out=None, stream=None, check: bool = False):
     """One sparse FFN layer on the GPU (see spb_ffn_forward in include/spb.h).
 
     w_gate / w_up / w_down: [f][d] rows (W_down stored transposed, as the
-    reference stores it); x [B][d] fp32; idx [B][f] fp32 labels (> 0 active).
+    reference stores it); x [B][d] fp32; the active sets either as idx [B][f]
+    fp32 labels (> 0 active) or as bits [B][ceil(f/32)] int32 words
+    (spb_ffn_forward_bits; f is then w_gate's row count unless given).
     check=True waits for the layer and raises if a bounded device wait ran
     out (the workspace's error word, which it then clears).
     """
     import torch
-    _require_cuda(w_gate, w_up, w_down, x, idx, out, merge_idx_out, count_out)
+    _require_cuda(w_gate, w_up, w_down, x, idx, bits, out, merge_idx_out, count_out)
+    if (idx is None) == (bits is None):
+        raise SpbError("ffn_forward: give exactly one of idx (labels) and bits")
     B, d = x.shape
-    f = idx.shape[1]
+    if idx is not None:
+        f = idx.shape[1]
+    elif f is None:
+        f = w_gate.shape[0]
     if out is None:
         out = torch.empty((B, d), dtype=torch.float32, device=x.device)
     ws = workspace if workspace is not None else new_workspace(B, d, f, 0, x.device)
-    _check(lib().spb_ffn_forward(w_gate.data_ptr(), w_up.data_ptr(), w_down.data_ptr(), wtype, x.data_ptr(),
-                                 idx.data_ptr(), B, d, f, act, int(per_token_mask), path, out.data_ptr(),
-                                 _ptr(merge_idx_out), _ptr(count_out), ws.data_ptr(), ws.numel(),
-                                 _stream(stream)), "spb_ffn_forward")
+    fn, sets = (lib().spb_ffn_forward, idx) if idx is not None else (lib().spb_ffn_forward_bits, bits)
+    _check(fn(w_gate.data_ptr(), w_up.data_ptr(), w_down.data_ptr(), wtype, x.data_ptr(), sets.data_ptr(), B, d, f,
+              act, int(per_token_mask), path, out.data_ptr(), _ptr(merge_idx_out), _ptr(count_out), ws.data_ptr(),
+              ws.numel(), _stream(stream)), "spb_ffn_forward")
     if check:
         code = device_error(ws)
         if code:
@@ -190,29 +198,35 @@ def predict_workspace(B: int, D: int, f: int, device=None):
     return torch.empty(int(lib().spb_predict_workspace_bytes(B, D, f)), dtype=torch.uint8, device=device or "cuda")
 
 
-def predict(p1, p2, x, k: int = 0, threshold: float = 0.0, *, return_idx: bool = False, out=None, workspace=None,
-            stream=None):
+def predict(p1, p2, x, k: int = 0, threshold: float = 0.0, *, return_idx: bool = False, out=None, bits_out=None,
+            labels: bool = True, workspace=None, stream=None):
     """DejaVu predictor on the GPU (spb_predict): labels [B][f] (1 active).
 
     p1 [D][d] fp16, p2 [f][D] fp16, x [B][d] fp32.  k > 0 selects the top-k
     logits per token; k = 0 thresholds the logits.  With return_idx, also the
     ascending active ids [B][k or f] and the per-token counts.  `out` ([B][f]
     fp32) and `workspace` (predict_workspace) make the call allocation-free,
-    so it can be captured in a CUDA graph.
+    so it can be captured in a CUDA graph.  bits_out ([B][ceil(f/32)] int32)
+    also receives the sets as bit words (the input of ffn_forward(bits=...));
+    labels=False skips the [B][f] label output and returns bits_out.
     """
     import torch
     _require_cuda(p1, p2, x, out, workspace)
     B, d = x.shape
     D, f = p1.shape[0], p2.shape[0]
     dev = x.device
-    labels = out if out is not None else torch.empty((B, f), dtype=torch.float32, device=dev)
+    _require_cuda(bits_out)
+    lab_t = (out if out is not None else torch.empty((B, f), dtype=torch.float32, device=dev)) if labels else None
+    if lab_t is None and bits_out is None:
+        raise SpbError("predict: labels=False needs bits_out")
     idx = torch.full((B, k if k > 0 else f), -1, dtype=torch.int32, device=dev) if return_idx else None
     counts = torch.zeros(B, dtype=torch.int32, device=dev) if return_idx else None
     ws = workspace if workspace is not None else predict_workspace(B, D, f, dev)
     _check(lib().spb_predict(p1.data_ptr(), p2.data_ptr(), x.data_ptr(), B, d, D, f, k, threshold,
-                             labels.data_ptr(), _ptr(idx), _ptr(counts), None, ws.data_ptr(), ws.numel(),
+                             _ptr(lab_t), _ptr(bits_out), _ptr(idx), _ptr(counts), None, ws.data_ptr(), ws.numel(),
                              _stream(stream)), "spb_predict")
-    return (labels, idx, counts) if return_idx else labels
+    res = lab_t if lab_t is not None else bits_out
+    return (res, idx, counts) if return_idx else res
 
 
 class dropin:

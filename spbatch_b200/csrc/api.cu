@@ -106,11 +106,16 @@ int spb_union(const float *idx, int B, int f, int group, int32_t *merge_idx, int
     return launch_compact(ws.seg_bits, S, f, merge_idx, act_cum, ws.counts, st);
 }
 
-int spb_ffn_forward(const void *w_gate, const void *w_up, const void *w_down, int wtype, const float *x,
-                    const float *idx, int B, int d, int f, int act, int per_token_mask, int path, float *out,
-                    int32_t *merge_idx_out, int32_t *count_out, void *workspace, size_t workspace_bytes,
-                    void *stream) {
-    if (!w_gate || !w_up || !w_down || !x || !idx || !out) return fail(SPB_ERR_INVALID, "spb_ffn_forward: null pointer");
+}  // extern "C"
+
+// The layer with the active sets either as fp32 labels (idx) or as per-token
+// bit words (tok_in); exactly one of the two is given.
+static int ffn_impl(const void *w_gate, const void *w_up, const void *w_down, int wtype, const float *x,
+                    const float *idx, const uint32_t *tok_in, int B, int d, int f, int act, int per_token_mask,
+                    int path, float *out, int32_t *merge_idx_out, int32_t *count_out, void *workspace,
+                    size_t workspace_bytes, void *stream) {
+    if (!w_gate || !w_up || !w_down || !x || (!idx && !tok_in) || !out)
+        return fail(SPB_ERR_INVALID, "spb_ffn_forward: null pointer");
     if (B <= 0 || d <= 0 || f <= 0) return fail(SPB_ERR_INVALID, "spb_ffn_forward: bad shape");
     if (d % 64 != 0) return fail(SPB_ERR_INVALID, "spb_ffn_forward: d must be a multiple of 64");
     if (B > 256) return fail(SPB_ERR_UNSUPPORTED, "spb_ffn_forward: B > 256");
@@ -142,6 +147,7 @@ int spb_ffn_forward(const void *w_gate, const void *w_up, const void *w_down, in
         L.wu = w_up;
         L.wd = w_down;
         L.labels = idx;
+        L.tok_in = tok_in;
         L.x = x;
         L.gbar = ws.gbar;
         L.x16 = ws.x16;
@@ -174,6 +180,7 @@ int spb_ffn_forward(const void *w_gate, const void *w_up, const void *w_down, in
         sa.wtype = wtype;
         sa.x = x;
         sa.idx = idx;
+        sa.tok_in = tok_in;
         sa.B = B;
         sa.d = d;
         sa.f = f;
@@ -205,7 +212,8 @@ int spb_ffn_forward(const void *w_gate, const void *w_up, const void *w_down, in
             sa.wd = w_down;
             sa.wtype = wtype;
             sa.x = x + (int64_t)t0 * d;
-            sa.idx = idx + (int64_t)t0 * f;
+            sa.idx = idx ? idx + (int64_t)t0 * f : nullptr;
+            sa.tok_in = tok_in ? tok_in + (int64_t)t0 * words_of(f) : nullptr;
             sa.B = B - t0 < chunk ? B - t0 : chunk;
             sa.d = d;
             sa.f = f;
@@ -225,7 +233,8 @@ int spb_ffn_forward(const void *w_gate, const void *w_up, const void *w_down, in
     PrepJobs jobs;
     jobs.zero_out = out;
     jobs.zero_n = (int64_t)B * d;
-    int rc = launch_union_bits(idx, B, f, B, ws.tok_bits, ws.seg_bits, jobs, st);
+    int rc = tok_in ? launch_union_from_bits(tok_in, B, f, B, ws.seg_bits, jobs, st)
+                    : launch_union_bits(idx, B, f, B, ws.tok_bits, ws.seg_bits, jobs, st);
     if (rc) return rc;
     FusedGemvArgs a{};
     a.wg = w_gate;
@@ -237,7 +246,7 @@ int spb_ffn_forward(const void *w_gate, const void *w_up, const void *w_down, in
     a.d = d;
     a.f = f;
     a.seg_bits = ws.seg_bits;
-    a.tok_bits = ws.tok_bits;
+    a.tok_bits = tok_in ? tok_in : ws.tok_bits;
     a.act = act;
     a.per_token = per_token_mask;
     a.h = ws.h;
@@ -248,15 +257,35 @@ int spb_ffn_forward(const void *w_gate, const void *w_up, const void *w_down, in
     return launch_fused_gemv(a, st);
 }
 
+extern "C" {
+
+int spb_ffn_forward(const void *w_gate, const void *w_up, const void *w_down, int wtype, const float *x,
+                    const float *idx, int B, int d, int f, int act, int per_token_mask, int path, float *out,
+                    int32_t *merge_idx_out, int32_t *count_out, void *workspace, size_t workspace_bytes,
+                    void *stream) {
+    if (!idx) return fail(SPB_ERR_INVALID, "spb_ffn_forward: null pointer");
+    return ffn_impl(w_gate, w_up, w_down, wtype, x, idx, nullptr, B, d, f, act, per_token_mask, path, out,
+                    merge_idx_out, count_out, workspace, workspace_bytes, stream);
+}
+
+int spb_ffn_forward_bits(const void *w_gate, const void *w_up, const void *w_down, int wtype, const float *x,
+                         const uint32_t *tok_bits, int B, int d, int f, int act, int per_token_mask, int path,
+                         float *out, int32_t *merge_idx_out, int32_t *count_out, void *workspace,
+                         size_t workspace_bytes, void *stream) {
+    if (!tok_bits) return fail(SPB_ERR_INVALID, "spb_ffn_forward_bits: null pointer");
+    return ffn_impl(w_gate, w_up, w_down, wtype, x, nullptr, tok_bits, B, d, f, act, per_token_mask, path, out,
+                    merge_idx_out, count_out, workspace, workspace_bytes, stream);
+}
+
 size_t spb_predict_workspace_bytes(int B, int D, int f) {
     if (B <= 0 || D <= 0 || f <= 0) return 0;
     return align256(sizeof(__half) * (size_t)B * D) + align256(sizeof(float) * (size_t)B * f);
 }
 
 int spb_predict(const void *p1, const void *p2, const float *x, int B, int d, int D, int f, int k, float threshold,
-                float *labels_out, int32_t *idx_out, int32_t *count_out, float *logits_out, void *workspace,
-                size_t workspace_bytes, void *stream) {
-    if (!p1 || !p2 || !x || !labels_out) return fail(SPB_ERR_INVALID, "spb_predict: null pointer");
+                float *labels_out, uint32_t *bits_out, int32_t *idx_out, int32_t *count_out, float *logits_out,
+                void *workspace, size_t workspace_bytes, void *stream) {
+    if (!p1 || !p2 || !x || (!labels_out && !bits_out)) return fail(SPB_ERR_INVALID, "spb_predict: null pointer");
     if (B <= 0 || d <= 0 || D <= 0 || f <= 0 || k < 0) return fail(SPB_ERR_INVALID, "spb_predict: bad shape");
     if (d % 256 || D % 256) return fail(SPB_ERR_INVALID, "spb_predict: d and D must be multiples of 256");
     if (!aligned16(p1) || !aligned16(p2)) return fail(SPB_ERR_INVALID, "spb_predict: weights must be 16-byte aligned");
@@ -267,7 +296,8 @@ int spb_predict(const void *p1, const void *p2, const float *x, int B, int d, in
                                : reinterpret_cast<float *>(static_cast<char *>(workspace) +
                                                            align256(sizeof(__half) * (size_t)B * D));
     return launch_predict(static_cast<const __half *>(p1), static_cast<const __half *>(p2), x, B, d, D, f, k,
-                          threshold, labels_out, idx_out, count_out, logits, hidden, static_cast<cudaStream_t>(stream));
+                          threshold, labels_out, bits_out, idx_out, count_out, logits, hidden,
+                          static_cast<cudaStream_t>(stream));
 }
 
 int spb_trace_enable(void *device_buffer, size_t slots) {

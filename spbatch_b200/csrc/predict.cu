@@ -183,7 +183,7 @@ __device__ __forceinline__ int sel_block_scan(int v, int *warp_tot, int *total) 
 // ids first) and the active ids in index order.
 __global__ void __launch_bounds__(kSelThreads)
 pred_select_kernel(const float *__restrict__ logits, int f, int k, float threshold, float *__restrict__ labels,
-                   int32_t *__restrict__ idx, int cap, int32_t *__restrict__ counts) {
+                   uint32_t *__restrict__ bits, int32_t *__restrict__ idx, int cap, int32_t *__restrict__ counts) {
     extern __shared__ uint32_t keys[];  // [f], then [kSelWarps][256] per-warp histograms
     uint32_t *whist = keys + ((f + 3) & ~3);
     __shared__ uint32_t hist[256];
@@ -281,8 +281,9 @@ pred_select_kernel(const float *__restrict__ logits, int f, int k, float thresho
     }
     const uint32_t thr_key = sel_prefix;
     const int take_eq = need;  // how many keys equal to thr_key are active (lowest ids first)
-    // contiguous index run of this thread
-    const int per = (f + kSelThreads - 1) / kSelThreads;
+    // contiguous index run of this thread, whole 32-neuron words so that the
+    // thread writes its bit words alone
+    const int per = 32 * ((f + 32 * kSelThreads - 1) / (32 * kSelThreads));
     const int j0 = min(f, (int)threadIdx.x * per), j1 = min(f, j0 + per);
     int n_eq = 0;
     if (topk)
@@ -300,12 +301,19 @@ pred_select_kernel(const float *__restrict__ logits, int f, int k, float thresho
     __syncthreads();
     int pos = sel_block_scan(n_act, warp_tot, &tot);
     eq_rank -= n_eq;  // replay the same decisions, now writing
+    const int W = (f + 31) / 32;
+    uint32_t word = 0;
     for (int j = j0; j < j1; ++j) {
         bool active;
         if (k >= f) active = true;
         else if (k > 0) active = keys[j] > thr_key || (keys[j] == thr_key && eq_rank++ < take_eq);
         else active = lg[j] >= threshold;
-        labels[(int64_t)t * f + j] = active ? 1.0f : 0.0f;
+        if (labels) labels[(int64_t)t * f + j] = active ? 1.0f : 0.0f;
+        word |= (active ? 1u : 0u) << (j & 31);
+        if (bits && ((j & 31) == 31 || j == j1 - 1)) {
+            bits[(int64_t)t * W + (j >> 5)] = word;
+            word = 0;
+        }
         if (active) {
             if (idx && pos < cap) idx[(int64_t)t * cap + pos] = j;
             ++pos;
@@ -315,8 +323,8 @@ pred_select_kernel(const float *__restrict__ logits, int f, int k, float thresho
 }
 
 int launch_predict(const __half *p1, const __half *p2, const float *x, int B, int d, int D, int f, int k,
-                   float threshold, float *labels, int32_t *idx, int32_t *counts, float *logits, __half *hidden,
-                   cudaStream_t st) {
+                   float threshold, float *labels, uint32_t *bits, int32_t *idx, int32_t *counts, float *logits,
+                   __half *hidden, cudaStream_t st) {
     const int sms = num_sms();
     const int ty = (B + kPredTokens - 1) / kPredTokens;
     {
@@ -348,7 +356,7 @@ int launch_predict(const __half *p1, const __half *p2, const float *x, int B, in
         if (smem > 200 * 1024) return fail(SPB_ERR_UNSUPPORTED, "spb_predict: f too large");
         if (int rc = ensure_smem((const void *)pred_select_kernel, smem)) return rc;
         const int cap = k > 0 ? k : f;
-        pred_select_kernel<<<B, kSelThreads, smem, st>>>(logits, f, k, threshold, labels, idx, cap, counts);
+        pred_select_kernel<<<B, kSelThreads, smem, st>>>(logits, f, k, threshold, labels, bits, idx, cap, counts);
         SPB_LAUNCH_CHECK("pred_select_kernel");
     }
     return SPB_OK;

@@ -57,7 +57,7 @@ struct Workspace {
     int32_t *counts;       // [S + 1] per-segment counts (+1 spare)
     __half *h;             // [f][B] fp16 intermediate of the CUDA-core path
     __half *x16;           // [Np][d] fp16 activations of the tensor path
-    unsigned int *gbar;    // [2] tensor path: grid barrier (arrival count, generation)
+    unsigned int *gbar;    // [3] tensor path: per-launch counters (barrier arrivals, prepared CTAs, finished CTAs)
     uint32_t *ready;       // [kMaxTcGrid / 2] tensor path: per-cluster h-publication counters (zeroed per launch)
     __half *h16;           // [Np][fpad] tensor path: fp16 h, K-major per token
     float *xchg;           // [kMaxTcGrid][Np][64] tensor path: per-CTA gate/up exchange slots

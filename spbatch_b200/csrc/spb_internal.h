@@ -22,6 +22,9 @@ struct PrepJobs {
 };
 int launch_union_bits(const float *idx, int B, int f, int G, uint32_t *tok_bits, uint32_t *seg_bits,
                       const PrepJobs &jobs, cudaStream_t st);
+// union words from per-token bits [B][W] (segments of G tokens)
+int launch_union_from_bits(const uint32_t *tok_in, int B, int f, int G, uint32_t *seg_bits, const PrepJobs &jobs,
+                           cudaStream_t st);
 int launch_compact(const uint32_t *seg_bits, int S, int f, int32_t *merge_idx, int32_t *act_cum, int32_t *counts,
                    cudaStream_t st);
 
@@ -48,7 +51,8 @@ struct StreamFfnArgs {
     const void *wg, *wu, *wd;  // [f][d] rows, format wtype
     int wtype;
     const float *x;            // [B][d]
-    const float *idx;          // [B][f] labels, active if > 0
+    const float *idx;          // [B][f] labels, active if > 0 (or null with tok_in)
+    const uint32_t *tok_in;    // [B][W] per-token activity bits, or null
     int B, d, f, act, per_token;
     int32_t *merge_out;        // [f] optional: ascending union ids
     int32_t *count_out;        // [1] optional: union size
@@ -109,7 +113,7 @@ const DebugHooks &debug_hooks();
 
 // predict.cu -- low-rank activity predictor
 int launch_predict(const __half *p1, const __half *p2, const float *x, int B, int d, int D, int f, int k,
-                   float threshold, float *labels, int32_t *idx, int32_t *counts, float *logits, __half *hidden,
-                   cudaStream_t st);
+                   float threshold, float *labels, uint32_t *bits, int32_t *idx, int32_t *counts, float *logits,
+                   __half *hidden, cudaStream_t st);
 
 }  // namespace spb

@@ -74,7 +74,8 @@ struct SfCtl {
 struct SfArgs {
     const uint8_t *wg, *wu, *wd;  // [f] rows of rb bytes
     const float *x;               // [B][d]
-    const float *idx;             // [B][f]
+    const float *idx;             // [B][f] labels, or null with tok_in
+    const uint32_t *tok_in;       // [B][W] per-token activity bits, or null
     float *out;                   // [B][d]
     int32_t *merge;               // [f] or null
     int32_t *count;               // [1] or null
@@ -286,7 +287,21 @@ __global__ void __launch_bounds__(kSfThreads, 1) stream_ffn_kernel(const SfArgs 
     // ---- the batch union: union words [W] and token words [NT][W] ----
     uint32_t *ubits = reinterpret_cast<uint32_t *>(smem + a.off_bits);
     uint32_t *tbits = ubits + a.W;
-    if (a.local_union) {
+    if (a.tok_in) {
+        // Per-token bits from the caller: every CTA reads the B x W words
+        // (1.4 KB per token at f = 11008) through L2 -- no grid-wide step.
+        for (int w = tid; w < a.W; w += kSfThreads) {
+            const uint32_t last = (w == a.W - 1 && (a.f & 31)) ? (1u << (a.f & 31)) - 1u : ~0u;
+            uint32_t un = 0;
+#pragma unroll
+            for (int t = 0; t < NT; ++t) {
+                const uint32_t bt = t < a.B ? (__ldg(a.tok_in + (int64_t)t * a.W + w) & last) : 0u;
+                if (t < a.B) tbits[t * a.W + w] = bt;
+                un |= bt;
+            }
+            ubits[w] = un;
+        }
+    } else if (a.local_union) {
         // One token: every CTA reads the whole label row (f fp32, active if
         // > 0) through L2 and builds the words itself -- no grid-wide step.
         if ((a.f & 3) == 0 && (reinterpret_cast<uintptr_t>(a.idx) & 15u) == 0) {
@@ -649,6 +664,7 @@ int launch_sf(const StreamFfnArgs &fa, cudaStream_t st) {
     a.wd = static_cast<const uint8_t *>(fa.wd);
     a.x = fa.x;
     a.idx = fa.idx;
+    a.tok_in = fa.tok_in;
     a.out = fa.out;
     a.merge = fa.merge_out;
     a.count = fa.count_out;
@@ -656,7 +672,7 @@ int launch_sf(const StreamFfnArgs &fa, cudaStream_t st) {
     a.seg_bits = fa.seg_bits;
     a.tok_bits = fa.tok_bits;
     a.grid_bar = fa.grid_bar;
-    a.local_union = fa.B == 1;
+    a.local_union = fa.B == 1 || fa.tok_in != nullptr;
     a.launch_ctr = fa.launch_ctr;
     a.zero_flag = fa.zero_flag;
     a.B = fa.B;
@@ -695,15 +711,16 @@ int launch_sf(const StreamFfnArgs &fa, cudaStream_t st) {
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     // programmatic dependent launch: the launch overlaps the previous
-    // kernel's tail; the kernel waits for it before touching global memory
-    // (several tokens: cooperative, for the grid barrier)
+    // kernel's tail; the kernel waits for it before touching global memory.
+    // Cooperative: CTAs wait for CTA 0's zeroed output (and, with several
+    // labelled tokens, for the grid barrier), so all of them must be resident.
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     attr[1].id = cudaLaunchAttributeCooperative;
     attr[1].val.cooperative = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = a.local_union ? 1 : 2;
+    cfg.numAttrs = 2;
     SPB_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, a));
     return SPB_OK;
 }

@@ -109,7 +109,9 @@ struct TcArgs {
     __half *x16;                 // [Np][d] fp16 activations (rows >= B zero), written in phase 0
     __half *h16;                 // [Np][fpad] h, K-major per token
     uint32_t *seg_bits;          // [W] batch union, written in phase 0
-    unsigned int *gbar;          // [2] grid barrier: arrival count, generation
+    unsigned int *gbar;          // [3] per-launch counters: grid-barrier arrivals, CTAs whose share of
+                                 // the activations / zeroed output is written, CTAs done (zero on entry;
+                                 // the last CTA to finish resets them and the cluster counters)
     float *out;                  // [B][d], zero on entry
     int32_t *merge_out;          // [f]
     int32_t *count_out;          // [1]
@@ -337,9 +339,37 @@ ffn_tc_kernel(const __grid_constant__ TcMaps maps, const TcArgs a) {
     // workspace) becomes visible here.
     grid_dependency_wait();
     if (tid == 0) stamp(a, kTrStart);
-    // ---- phase 0, shared by all CTAs: union bits, fp16 activations, zeroed
-    // output and counters; then one grid barrier.
-    {
+    // ---- phase 0.  Labels: every CTA computes a share of the union words,
+    // the fp16 activations and the zeroed output, then one grid barrier.
+    // Bits (tok_in): every CTA ORs the caller's per-token words itself (B x W
+    // words through L2) and needs no grid-wide step; its share of the
+    // activations and of the zeroed output is published on a counter that
+    // only the activation loads and the first output reduction wait for.
+    const bool bits_in = a.tok_in != nullptr;
+    if (bits_in) {
+        for (int w = tid; w < W; w += kTcThreads) {
+            uint32_t u = 0;
+            const uint32_t *col = a.tok_in + w;
+#pragma unroll 8
+            for (int t = 0; t < a.B; ++t) u |= __ldg(col + (int64_t)t * W);
+            if (w == W - 1 && (a.f & 31)) u &= (1u << (a.f & 31)) - 1u;
+            bits[w] = u;
+        }
+        const int64_t gt = (int64_t)blockIdx.x * kTcThreads + tid, gs = (int64_t)gridDim.x * kTcThreads;
+        const int64_t n2 = (int64_t)Np * a.d / 2;
+        for (int64_t i = gt; i < n2; i += gs) {
+            const int t = (int)((2 * i) / a.d);
+            const float2 v = t < a.B ? *reinterpret_cast<const float2 *>(a.x + 2 * i) : make_float2(0.f, 0.f);
+            reinterpret_cast<__half2 *>(a.x16)[i] = __floats2half2_rn(v.x, v.y);
+        }
+        const int64_t n4 = (int64_t)a.B * a.d / 4;
+        for (int64_t i = gt; i < n4; i += gs) reinterpret_cast<float4 *>(a.out)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        __syncthreads();
+        if (tid == 0) {
+            __threadfence();
+            red_add_release_u32(a.gbar + 1, 1u);
+        }
+    } else {
         const int64_t gt = (int64_t)blockIdx.x * kTcThreads + tid, gs = (int64_t)gridDim.x * kTcThreads;
         const int64_t n2 = (int64_t)Np * a.d / 2;
         // the first two activation pairs of this thread are loaded before the
@@ -380,10 +410,8 @@ ffn_tc_kernel(const __grid_constant__ TcMaps maps, const TcArgs a) {
         }
         const int64_t n4 = (int64_t)a.B * a.d / 4;
         for (int64_t i = gt; i < n4; i += gs) reinterpret_cast<float4 *>(a.out)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (gt < nclu) a.ready[gt] = 0u;
         if (tid == 0) stamp(a, kTrPhase0);
-        // grid barrier: gbar[0] counts arrivals (zero on entry); the last CTA
-        // to leave resets both words for the next launch
+        // grid barrier on gbar[0] (arrivals)
         __syncthreads();
         if (tid == 0) {
             __threadfence();
@@ -396,15 +424,11 @@ ffn_tc_kernel(const __grid_constant__ TcMaps maps, const TcArgs a) {
                 }
                 __nanosleep(32);
             }
-            if (atomicAdd(a.gbar + 1, 1u) == gridDim.x - 1) {
-                a.gbar[0] = 0u;
-                a.gbar[1] = 0u;
-            }
         }
         __syncthreads();
+        if (tid == 0) stamp(a, kTrBarrier);
+        for (int w = tid; w < W; w += kTcThreads) bits[w] = __ldcg(a.seg_bits + w);
     }
-    if (tid == 0) stamp(a, kTrBarrier);
-    for (int w = tid; w < W; w += kTcThreads) bits[w] = __ldcg(a.seg_bits + w);
     __syncthreads();
     scan_popc(bits, W, prefix, wtot);  // ends with __syncthreads
     if (tid == 0) stamp(a, kTrScan);
@@ -500,11 +524,12 @@ ffn_tc_kernel(const __grid_constant__ TcMaps maps, const TcArgs a) {
         // transaction barrier.
         if (lane == 0) {
             int t = 0;  // unit-step
-            // x16 was written by generic stores in phase 0; TMA reads through
-            // the async proxy
+            // x16 was written by generic stores in phase 0 (by every CTA when
+            // the sets came as bits); TMA reads through the async proxy
+            bool ok = !ctl->abort;
+            if (bits_in && ok) ok = wait_count(a.gbar + 1, gridDim.x, ctl, a);
             asm volatile("fence.proxy.async.global;" ::: "memory");
             const int rot = KG ? clu % KG : 0;
-            bool ok = !ctl->abort;
             for (int i = 0; i < ntile && ok; ++i) {
                 for (int st = 0; st < KG; ++st, t += GW) {
                     if (!(ok = ring_wait_empty(t, NU, ctl, a) && (GW == 1 || ring_wait_empty(t + 1, NU, ctl, a))))
@@ -779,9 +804,11 @@ ffn_tc_kernel(const __grid_constant__ TcMaps maps, const TcArgs a) {
         }
         if (e == 0) stamp(a, kTrHDone);
         if (ok && ndn > 0) {
-            // 4. the down unit: out[t][256 m + col] += acc
+            // 4. the down unit: out[t][256 m + col] += acc (once every CTA's
+            // share of `out` is zeroed)
             const int buf = ub % nbuf;
             ok = wait_bar(&ctl->acc_full[buf], (uint32_t)(ub / nbuf) & 1u, ctl, a, kErrTimeoutAcc, a.hint_acc);
+            if (ok && bits_in) ok = wait_count(a.gbar + 1, gridDim.x, ctl, a);
             if ((ok = named_bar_and(kEpiBar, 128, ok))) {
                 tc_fence_after();
                 if (e == 0) {
@@ -816,6 +843,17 @@ ffn_tc_kernel(const __grid_constant__ TcMaps maps, const TcArgs a) {
 
     __syncthreads();
     if (tid == 0) stamp(a, kTrEnd);
+    // The last CTA to finish resets the per-launch counters: every other CTA
+    // has passed all its waits on them.
+    if (tid == 0) {
+        __threadfence();
+        if (atomicAdd(a.gbar + 2, 1u) == gridDim.x - 1) {
+            for (int c = 0; c < nclu; ++c) a.ready[c] = 0u;
+            a.gbar[0] = 0u;
+            a.gbar[1] = 0u;
+            a.gbar[2] = 0u;
+        }
+    }
     // The partner may still signal this CTA's barriers until it is done.
     cluster_sync_all();
     if (warp == kMmaWarp) {

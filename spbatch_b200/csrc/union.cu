@@ -92,6 +92,31 @@ union_bits_kernel(const float *__restrict__ idx, int B, int f, int W, int G, uin
     }
 }
 
+// Union words from per-token bits: word w of segment s is the OR of the
+// tokens' words; also runs the same prep jobs as union_bits_kernel.
+__global__ void __launch_bounds__(kUnionWarps * 32)
+union_from_bits_kernel(const uint32_t *__restrict__ tok_in, int B, int f, int W, int G,
+                       uint32_t *__restrict__ seg_bits, PrepJobs jobs) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    const int64_t gtid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    const int S = (B + G - 1) / G;
+    for (int64_t i = gtid; i < (int64_t)S * W; i += stride) {
+        const int s = (int)(i / W), w = (int)(i % W);
+        uint32_t u = 0;
+        for (int t = s * G; t < min(B, (s + 1) * G); ++t) u |= __ldg(tok_in + (int64_t)t * W + w);
+        if (w == W - 1 && (f & 31)) u &= (1u << (f & 31)) - 1u;
+        seg_bits[i] = u;
+    }
+    if (jobs.zero_out) {
+        const int64_t n4 = jobs.zero_n / 4;
+        for (int64_t i = gtid; i < n4; i += stride)
+            reinterpret_cast<float4 *>(jobs.zero_out)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int64_t i = n4 * 4 + gtid; i < jobs.zero_n; i += stride) jobs.zero_out[i] = 0.0f;
+    }
+}
+
 constexpr int kCompactThreads = 1024;
 
 // CTA s compacts segment s.  act_cum[s] = number of active neurons in
@@ -152,6 +177,25 @@ int launch_union_bits(const float *idx, int B, int f, int G, uint32_t *tok_bits,
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     SPB_CUDA_TRY(cudaLaunchKernelEx(&cfg, union_bits_kernel, idx, B, f, W, G, tok_bits, seg_bits, jobs));
+    return SPB_OK;
+}
+
+int launch_union_from_bits(const uint32_t *tok_in, int B, int f, int G, uint32_t *seg_bits, const PrepJobs &jobs,
+                           cudaStream_t st) {
+    const int W = words_of(f);
+    const int S = (B + G - 1) / G;
+    int grid = (S * W + 255) / 256;
+    if (jobs.zero_out) grid = max(grid, num_sms());
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(max(1, grid));
+    cfg.blockDim = dim3(kUnionWarps * 32);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    SPB_CUDA_TRY(cudaLaunchKernelEx(&cfg, union_from_bits_kernel, tok_in, B, f, W, G, seg_bits, jobs));
     return SPB_OK;
 }
 

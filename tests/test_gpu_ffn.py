@@ -337,3 +337,45 @@ def test_gemv_70b_token_groups(spb, cuda, oracle_mod, B):
     torch.cuda.synchronize()
     assert _ws_error(ws) == 0
     assert_close(out.cpu().numpy(), oracle_mod.ffn(*W, x, lab))
+
+
+def _to_bits(lab):
+    """[B][f] labels -> [B][ceil(f/32)] int32 bit words (bit j % 32 of word j / 32)."""
+    b = np.packbits((lab > 0).astype(np.uint8), axis=1, bitorder="little")
+    b = np.pad(b, ((0, 0), (0, (-b.shape[1]) % 4)))
+    return np.ascontiguousarray(b.view(np.int32))
+
+
+@pytest.mark.parametrize("B,d,f,path", [(1, 4096, 11008, 1), (3, 1024, 2050, 1), (4, 8192, 3001, 1),
+                                        (6, 1024, 2050, 1), (8, 4096, 11008, 2), (32, 4096, 11008, 2),
+                                        (33, 1024, 1000, 2), (64, 1024, 4096, 2)])
+def test_bits_input_matches_labels(spb, cuda, oracle_mod, B, d, f, path):
+    """spb_ffn_forward_bits gives spb_ffn_forward's results (union exact,
+    outputs within tolerance of the oracle) on every path: streaming
+    (B <= 4), token groups (d = 8192 with B > 2, B > 4), tensor cores."""
+    import torch
+    rng = np.random.default_rng(1000 + B + f)
+    W = _layer(rng, d, f, 0.02 if d >= 4096 else 0.04)
+    x = rng.standard_normal((B, d)).astype(np.float32)
+    lab = zipf_active_labels(B, f, max(1, f // 10), seed=B + f)
+    Wd = [_dev(w, cuda) for w in W]
+    outs = []
+    for sets in ("labels", "bits"):
+        ws = spb.new_workspace(B, d, f, 0, cuda)
+        merge = torch.full((f,), -1, dtype=torch.int32, device=cuda)
+        count = torch.zeros(1, dtype=torch.int32, device=cuda)
+        kw = dict(idx=_dev(lab, cuda)) if sets == "labels" else dict(bits=_dev(_to_bits(lab), cuda))
+        want_idx = path == 2  # index outputs: tensor path (the streaming path writes them too for B <= 4)
+        out = spb.ffn_forward(*Wd, _dev(x, cuda), **kw, path=path, workspace=ws,
+                              merge_idx_out=merge if want_idx else None, count_out=count if want_idx else None)
+        torch.cuda.synchronize()
+        assert _ws_error(ws) == 0
+        if want_idx:
+            ref_idx = np.nonzero((lab > 0).any(0))[0]
+            U = int(count.cpu()[0])
+            assert U == len(ref_idx)
+            np.testing.assert_array_equal(merge.cpu().numpy()[:U], ref_idx)
+        outs.append(out.cpu().numpy())
+    want = oracle_mod.ffn(*W, x, lab)
+    (assert_close_70b if d >= 8192 else assert_close)(outs[0], want)
+    (assert_close_70b if d >= 8192 else assert_close)(outs[1], want)

@@ -30,13 +30,19 @@ def _run(spb, cuda, p1, p2, x, k, thr=0.0):
     idx = torch.full((B, cap), -1, dtype=torch.int32, device=cuda)
     counts = torch.zeros(B, dtype=torch.int32, device=cuda)
     logits = torch.empty((B, f), device=cuda)
+    bits = torch.full((B, (f + 31) // 32), -1, dtype=torch.int32, device=cuda)
     ws = torch.zeros(int(spb.lib().spb_predict_workspace_bytes(B, D, f)), dtype=torch.uint8, device=cuda)
     rc = spb.lib().spb_predict(P1.data_ptr(), P2.data_ptr(), X.data_ptr(), B, x.shape[1], D, f, k, thr,
-                               labels.data_ptr(), idx.data_ptr(), counts.data_ptr(), logits.data_ptr(), ws.data_ptr(),
-                               ws.numel(), torch.cuda.current_stream().cuda_stream)
+                               labels.data_ptr(), bits.data_ptr(), idx.data_ptr(), counts.data_ptr(), logits.data_ptr(),
+                               ws.data_ptr(), ws.numel(), torch.cuda.current_stream().cuda_stream)
     assert rc == 0, spb.lib().spb_last_error()
     torch.cuda.synchronize()
-    return logits.cpu().numpy(), labels.cpu().numpy(), idx.cpu().numpy(), counts.cpu().numpy()
+    lab = labels.cpu().numpy()
+    # the bit words hold exactly the label sets
+    want_bits = np.packbits((lab > 0).astype(np.uint8), axis=1, bitorder="little")
+    want_bits = np.pad(want_bits, ((0, 0), (0, (-want_bits.shape[1]) % 4))).view(np.uint32)
+    np.testing.assert_array_equal(bits.cpu().numpy().view(np.uint32), want_bits)
+    return logits.cpu().numpy(), lab, idx.cpu().numpy(), counts.cpu().numpy()
 
 
 @pytest.mark.parametrize("B,d,D,f,k", [(1, 4096, 1024, 11008, 1101), (4, 512, 256, 1000, 100), (19, 1024, 512, 2048, 300),
