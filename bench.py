@@ -400,26 +400,13 @@ def run_ours(a):
             del Wfull, parts
         dist.broadcast(ok, 0)
         shard_parity = bool(ok.item())
-        # the collective alone, on the compute stream
+    if sharded:
+        # the collective alone: 50 all-reduces of the [B][d] fp32 output
+        # captured in one graph, replayed on the compute stream
         buf = torch.zeros((a.batch, d), device=device)
-        ev = []
-        with torch.cuda.stream(stream):
-            for _ in range(5):
-                dist.all_reduce(buf)
-            for _ in range(50):
-                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                e0.record(stream)
-                dist.all_reduce(buf)
-                e1.record(stream)
-                ev.append((e0, e1))
-        torch.cuda.synchronize()
-        allreduce_us = statistics.median(e0.elapsed_time(e1) * 1e3 for e0, e1 in ev)
-    if sharded and allreduce_us is None:
-        buf = torch.zeros((a.batch, d), device=device)
-        with torch.cuda.stream(stream):
-            for _ in range(5):
-                dist.all_reduce(buf)
-        torch.cuda.synchronize()
+        art = Timer(torch, stream, 1, lambda i: dist.all_reduce(buf), graphs=True)
+        art.warm(3)
+        allreduce_us = art.time(50, 5, dist, device)[0] * 1e3
 
     # e2e: pinned host inputs copied in and the output copied back every step
     pinned = [dict(x=torch.from_numpy(ly["x_np"]).pin_memory(), lab=torch.from_numpy(ly["lab_np"]).pin_memory(),
@@ -487,10 +474,22 @@ def run_ours(a):
         rec["cpu_baseline"] = cpu_baseline(a, layers[0], Wl[0], budget=a.cpu_budget)
     if rank == 0:
         print(json.dumps(rec), flush=True)
-    if ws_n > 1:
-        dist.destroy_process_group()
+    code = 0
     if rec["device_error"]:
-        sys.exit(f"device error word {rec['device_error']}: a bounded device wait ran out; the run is invalid")
+        print(f"device error word {rec['device_error']}: a bounded device wait ran out; the run is invalid",
+              file=sys.stderr, flush=True)
+        code = 1
+    if ws_n > 1:
+        # All work is done and the line is printed.  CUDA graphs that captured
+        # NCCL calls are still alive here, and tearing the process group down
+        # under them can block; every rank leaves after a final barrier.
+        torch.cuda.synchronize()
+        dist.barrier()
+        sys.stdout.flush()
+        sys.stderr.flush()
+        os._exit(code)
+    if code:
+        sys.exit(code)
 
 
 def config_dict(a, d, f, f_shard, k, Us, Us_full, L, bytes_step, ws_n, sharded):

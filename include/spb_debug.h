@@ -25,7 +25,7 @@ enum {
     SPB_DEBUG_TC_STAGES = 4,  /* tensor path: cap on the ring depth (0 automatic) */
     SPB_DEBUG_TC_HINT_ACC = 5, /* tensor path: suspend hint of the epilogue's accumulator waits, ns */
     SPB_DEBUG_TC_HINT = 6,    /* tensor path: suspend hint of the ring waits, ns */
-    SPB_DEBUG_TC_SPLIT_STAGES = 7, /* tensor path: 1 = gate/up stages over two ring units */
+    SPB_DEBUG_TC_SPLIT_STAGES = 7, /* tensor path: 1 = one ring unit per stage (no half-stage units) */
 };
 
 /* Sets one process-wide hook; applies to launches made after the call. */

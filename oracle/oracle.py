@@ -31,13 +31,22 @@ _lib = None
 _ref = None
 
 
+def ref_dir() -> str | None:
+    """The reference checkout: $SPB_REF_DIR, else a `reference` directory next
+    to this repository; None when neither holds the reference's cuda/ sources."""
+    cand = os.environ.get("SPB_REF_DIR") or os.path.join(os.path.dirname(HERE), os.pardir, "reference")
+    cand = os.path.abspath(cand)
+    return cand if os.path.isdir(os.path.join(cand, "cuda")) else None
+
+
 def build(ref: bool = False) -> None:
     """Compile the oracle (and the reference library when asked and possible)."""
     subprocess.check_call(["make", "-s", "-C", HERE, "all"])
-    if ref and os.path.isdir("/root/reference/cuda"):
-        subprocess.check_call(["make", "-s", "-C", HERE, "ref"])
-        # the reference's spmm_test driver against this library and its own
-        subprocess.check_call(["make", "-s", "-C", HERE, "drivers"])
+    rd = ref_dir() if ref else None
+    if rd:
+        subprocess.check_call(["make", "-s", "-C", HERE, "ref", f"REF_DIR={rd}"])
+        # the reference's spmm_test / ffn_test drivers against this library and its own
+        subprocess.check_call(["make", "-s", "-C", HERE, "drivers", f"REF_DIR={rd}"])
 
 
 def lib():

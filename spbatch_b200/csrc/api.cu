@@ -277,9 +277,37 @@ int spb_ffn_forward_bits(const void *w_gate, const void *w_up, const void *w_dow
                     merge_idx_out, count_out, workspace, workspace_bytes, stream);
 }
 
+// Predictor workspace: fp16 hidden [B][D], fp32 logits [B][f], then the
+// select's scratch (PredScratch).
+static size_t predict_layout(int B, int D, int f, char *base, __half **hidden, float **logits, PredScratch *sc) {
+    size_t off = 0;
+    auto take = [&](size_t n) {
+        char *p = base ? base + off : nullptr;
+        off += align256(n);
+        return p;
+    };
+    char *h = take(sizeof(__half) * (size_t)B * D);
+    char *l = take(sizeof(float) * (size_t)B * f);
+    char *hi = take(sizeof(uint32_t) * 2048 * (size_t)B);
+    char *ca = take(sizeof(uint2) * (size_t)B * f);
+    char *cc = take(sizeof(uint32_t) * (size_t)B);
+    char *se = take(sizeof(int2) * (size_t)B);
+    char *bi = take(sizeof(uint32_t) * (size_t)B * words_of(f));
+    if (base) {
+        *hidden = reinterpret_cast<__half *>(h);
+        *logits = reinterpret_cast<float *>(l);
+        sc->hist = reinterpret_cast<uint32_t *>(hi);
+        sc->cand = reinterpret_cast<uint2 *>(ca);
+        sc->cand_cnt = reinterpret_cast<uint32_t *>(cc);
+        sc->sel = reinterpret_cast<int2 *>(se);
+        sc->bits = reinterpret_cast<uint32_t *>(bi);
+    }
+    return off;
+}
+
 size_t spb_predict_workspace_bytes(int B, int D, int f) {
     if (B <= 0 || D <= 0 || f <= 0) return 0;
-    return align256(sizeof(__half) * (size_t)B * D) + align256(sizeof(float) * (size_t)B * f);
+    return predict_layout(B, D, f, nullptr, nullptr, nullptr, nullptr);
 }
 
 int spb_predict(const void *p1, const void *p2, const float *x, int B, int d, int D, int f, int k, float threshold,
@@ -291,12 +319,13 @@ int spb_predict(const void *p1, const void *p2, const float *x, int B, int d, in
     if (!aligned16(p1) || !aligned16(p2)) return fail(SPB_ERR_INVALID, "spb_predict: weights must be 16-byte aligned");
     const size_t need = spb_predict_workspace_bytes(B, D, f);
     if (!workspace || workspace_bytes < need) return fail(SPB_ERR_WORKSPACE, "spb_predict: workspace too small");
-    __half *hidden = static_cast<__half *>(workspace);
-    float *logits = logits_out ? logits_out
-                               : reinterpret_cast<float *>(static_cast<char *>(workspace) +
-                                                           align256(sizeof(__half) * (size_t)B * D));
+    __half *hidden = nullptr;
+    float *logits = nullptr;
+    PredScratch sc{};
+    predict_layout(B, D, f, static_cast<char *>(workspace), &hidden, &logits, &sc);
+    if (logits_out) logits = logits_out;
     return launch_predict(static_cast<const __half *>(p1), static_cast<const __half *>(p2), x, B, d, D, f, k,
-                          threshold, labels_out, bits_out, idx_out, count_out, logits, hidden,
+                          threshold, labels_out, bits_out, idx_out, count_out, logits, hidden, sc,
                           static_cast<cudaStream_t>(stream));
 }
 

@@ -5,6 +5,8 @@
 #include <mutex>
 #include <unordered_map>
 
+#include <vector>
+
 #include "spb_internal.h"
 #include "spbatch/kernel.cuh"
 
@@ -280,6 +282,18 @@ void up_mul_mat_cuda_sparse(const half *weight, const float *input, float *dst, 
                                SPARSITY_GROUP_SIZE, stream));
 }
 
+// One reusable event per device and host thread for ordering stream1 after
+// stream0 (cudaStreamWaitEvent captures the event's state at call time, so
+// re-recording it later is safe).
+static cudaEvent_t ordering_event() {
+    thread_local std::vector<cudaEvent_t> events;
+    int dev = 0;
+    CUDA_CHECK(cudaGetDevice(&dev));
+    if ((int)events.size() <= dev) events.resize(dev + 1, nullptr);
+    if (!events[dev]) CUDA_CHECK(cudaEventCreateWithFlags(&events[dev], cudaEventDisableTiming));
+    return events[dev];
+}
+
 void gate_and_up_mul_mat_cuda_sparse(const half *gate_w, const half *up_w, const float *input, float *gate_dst,
                                      float *up_dst, int *merge_idx, const int M, const int N, const int K,
                                      const int *act_neurons_device, cudaStream_t stream0, cudaStream_t stream1) {
@@ -294,11 +308,9 @@ void gate_and_up_mul_mat_cuda_sparse(const half *gate_w, const half *up_w, const
     if (stream1 != stream0) {
         // The reference computes up on stream1; order stream1 after the fused
         // launch so work queued there sees up_dst.
-        cudaEvent_t ev;
-        CUDA_CHECK(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+        cudaEvent_t ev = ordering_event();
         CUDA_CHECK(cudaEventRecord(ev, stream0));
         CUDA_CHECK(cudaStreamWaitEvent(stream1, ev, 0));
-        CUDA_CHECK(cudaEventDestroy(ev));
     }
 }
 

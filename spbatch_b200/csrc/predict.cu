@@ -26,15 +26,15 @@ namespace spb {
 
 constexpr int kPredThreads = 256;
 constexpr int kPredWarps = kPredThreads / 32;
-constexpr int kPredTokens = 8;  // tokens per CTA (activations staged in shared memory)
+// Tokens per CTA (their activations staged in shared memory) are a template
+// parameter: one at B = 1 (fewest registers), eight otherwise.
 
 // Fixed-order dot of one fp16 row (n values, n % 256 == 0) with nt vectors
 // held in shared memory as fp32 (stride n); result broadcast to all lanes.
-template <int NT>
+template <int NT, int kBatch = 8>  // kBatch: 16-byte loads in flight per lane (the FMA order is unchanged)
 __device__ __forceinline__ void fixed_dot(const __half *__restrict__ row, const __half *__restrict__ vs, int n,
                                           int nt, float (&acc)[NT]) {
     const int lane = threadIdx.x & 31;
-    constexpr int kBatch = 8;  // 16-byte loads in flight per lane (the FMA order is unchanged)
 #pragma unroll
     for (int t = 0; t < NT; ++t) acc[t] = 0.0f;
     const int nch = n / 8;
@@ -85,12 +85,44 @@ __device__ __forceinline__ void fixed_dot(const __half *__restrict__ row, const 
     }
 }
 
-// hidden[t][r], grid (ceil(D / rows), ceil(B / kPredTokens)).
+constexpr int kHistBins = 2048;  // logit histogram: the top 11 bits of the order key
+
+// Programmatic dependent launch: each predictor kernel is launched while the
+// previous one drains, waits for its results (griddepcontrol.wait) before
+// reading them, and lets its own successor launch early.
+__device__ __forceinline__ void pdl_enter() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+template <typename... KArgs, typename... Args>
+static int launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, const char *what,
+                      Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+    if (e != cudaSuccess) return cuda_fail(e, what);
+    return SPB_OK;
+}
+
+// hidden[t][r], grid (ceil(D / rows), ceil(B / NT)); the first CTA column
+// also zeroes the tokens' logit histograms.  KB: loads in flight per lane
+// (16 holds a whole 8 KB row at d = 4096).
+template <int NT, int KB>
 __global__ void __launch_bounds__(kPredThreads)
 pred_hidden_kernel(const __half *__restrict__ p1, const float *__restrict__ x, __half *__restrict__ hidden, int B,
-                   int d, int D, int rows_per_cta) {
-    extern __shared__ __align__(16) __half xs[];  // [kPredTokens][d], fp16-rounded x
-    const int t0 = blockIdx.y * kPredTokens, nt = min(kPredTokens, B - t0);
+                   int d, int D, int rows_per_cta, uint32_t *__restrict__ hist, uint32_t *__restrict__ cand_cnt) {
+    extern __shared__ __align__(16) __half xs[];  // [NT][d], fp16-rounded x
+    pdl_enter();
+    const int t0 = blockIdx.y * NT, nt = min(NT, B - t0);
     {  // float4 loads, several in flight per thread (d % 256 == 0)
         const float4 *src = reinterpret_cast<const float4 *>(x + (int64_t)t0 * d);
         const int n4 = nt * d / 4;
@@ -114,23 +146,37 @@ pred_hidden_kernel(const __half *__restrict__ p1, const float *__restrict__ x, _
             }
         }
     }
+    if (hist && blockIdx.x == 0) {
+        for (int i = threadIdx.x; i < nt * kHistBins; i += blockDim.x) hist[(int64_t)t0 * kHistBins + i] = 0u;
+        if (cand_cnt && threadIdx.x < nt) cand_cnt[t0 + threadIdx.x] = 0u;
+    }
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int r1 = min(D, (int)(blockIdx.x + 1) * rows_per_cta);
     for (int r = blockIdx.x * rows_per_cta + warp; r < r1; r += kPredWarps) {
-        float acc[kPredTokens];
-        fixed_dot<kPredTokens>(p1 + (int64_t)r * d, xs, d, nt, acc);
+        float acc[NT];
+        fixed_dot<NT, KB>(p1 + (int64_t)r * d, xs, d, nt, acc);
         if (lane == 0)
             for (int t = 0; t < nt; ++t) hidden[(int64_t)(t0 + t) * D + r] = __float2half_rn(fmaxf(acc[t], 0.0f));
     }
 }
 
-// logit[t][j], grid (ceil(f / rows), ceil(B / kPredTokens)).
+// Order-preserving map of an fp32 logit to an unsigned key.
+__device__ __forceinline__ uint32_t order_key(float v) {
+    const uint32_t b = __float_as_uint(v);
+    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
+// logit[t][j], grid (ceil(f / rows), ceil(B / NT)).  With `hist` (top-k
+// selection) it also counts each logit in its token's histogram of the top
+// 11 bits of the order key, so the select skips a full pass.
+template <int NT>
 __global__ void __launch_bounds__(kPredThreads)
 pred_logit_kernel(const __half *__restrict__ p2, const __half *__restrict__ hidden, float *__restrict__ logits, int B,
-                  int D, int f, int rows_per_cta) {
-    extern __shared__ __align__(16) __half hs[];  // [kPredTokens][D]
-    const int t0 = blockIdx.y * kPredTokens, nt = min(kPredTokens, B - t0);
+                  int D, int f, int rows_per_cta, uint32_t *__restrict__ hist) {
+    extern __shared__ __align__(16) __half hs[];  // [NT][D]
+    pdl_enter();
+    const int t0 = blockIdx.y * NT, nt = min(NT, B - t0);
     {  // 8 fp16 values per 16-byte load (D % 256 == 0)
         const uint4 *src = reinterpret_cast<const uint4 *>(hidden + (int64_t)t0 * D);
         const int n8 = nt * D / 8;
@@ -140,17 +186,17 @@ pred_logit_kernel(const __half *__restrict__ p2, const __half *__restrict__ hidd
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int j1 = min(f, (int)(blockIdx.x + 1) * rows_per_cta);
     for (int j = blockIdx.x * rows_per_cta + warp; j < j1; j += kPredWarps) {
-        float acc[kPredTokens];
-        fixed_dot<kPredTokens>(p2 + (int64_t)j * D, hs, D, nt, acc);
-        if (lane == 0)
-            for (int t = 0; t < nt; ++t) logits[(int64_t)(t0 + t) * f + j] = acc[t];
+        float acc[NT];
+        fixed_dot<NT, 8>(p2 + (int64_t)j * D, hs, D, nt, acc);
+        if (lane < nt) {  // lane t records token t (every lane holds every sum)
+            float v = acc[0];
+#pragma unroll
+            for (int t = 1; t < NT; ++t)
+                if (lane == t) v = acc[t];
+            logits[(int64_t)(t0 + lane) * f + j] = v;
+            if (hist) atomicAdd(hist + (int64_t)(t0 + lane) * kHistBins + (order_key(v) >> 21), 1u);
+        }
     }
-}
-
-// Order-preserving map of an fp32 logit to an unsigned key.
-__device__ __forceinline__ uint32_t order_key(float v) {
-    const uint32_t b = __float_as_uint(v);
-    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
 }
 
 constexpr int kSelThreads = 1024;
@@ -174,6 +220,72 @@ __device__ __forceinline__ int sel_block_scan(int v, int *warp_tot, int *total) 
     return warp_tot[warp] + incl - v;
 }
 
+// Radix narrowing over src[0..n): for each 8-bit digit at shift0, then
+// (13 -> 5 -> 0 or 24 -> 16 -> 8 -> 0), the keys matching (*prefix, *mask)
+// are counted per digit and the digit holding the *need-th largest key is
+// appended; on return *prefix is that key and *need the number of keys equal
+// to it that belong to the top set.  Whole block (kSelThreads threads).
+__device__ void radix_narrow(const uint32_t *src, int n, int shift0, uint32_t *whist, uint32_t *bins,
+                             uint32_t *sel_prefix, uint32_t *sel_mask, int *need) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    for (int shift = shift0; shift >= 0; shift = shift == 13 ? 5 : (shift == 5 ? 0 : shift - 8)) {
+        // per-warp histograms: logits crowd into a few bins, so a shared
+        // histogram would serialise the whole block on those counters
+        for (int i = threadIdx.x; i < kSelWarps * 256; i += blockDim.x) whist[i] = 0u;
+        __syncthreads();
+        const uint32_t pfx = *sel_prefix, msk = *sel_mask;
+        uint32_t *wh = whist + warp * 256;
+        for (int j = threadIdx.x; j < n; j += blockDim.x) {
+            const uint32_t key = src[j];
+            if ((key & msk) == pfx) atomicAdd(&wh[(key >> shift) & 255u], 1u);
+        }
+        __syncthreads();
+        if (threadIdx.x < 256) {
+            uint32_t sum = 0;
+            for (int w = 0; w < kSelWarps; ++w) sum += whist[w * 256 + threadIdx.x];
+            bins[threadIdx.x] = sum;
+        }
+        __syncthreads();
+        if (warp == 0) {
+            // lane l holds bins 255-8l .. 248-8l (descending); the answer is
+            // the highest bin b with (count of bins > b) < need <= (count of bins >= b)
+            uint32_t c[8], sum = 0;
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                c[q] = bins[255 - 8 * lane - q];
+                sum += c[q];
+            }
+            uint32_t incl = sum;  // inclusive scan over lanes (descending bins)
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint32_t nn = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += nn;
+            }
+            const int rem = *need;
+            uint32_t before = incl - sum;  // keys in higher bins than this lane's
+            int found = -1, rem_out = 0;
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                if (found < 0 && (int)(before + c[q]) >= rem) {
+                    found = 255 - 8 * lane - q;
+                    rem_out = rem - (int)before;
+                }
+                before += c[q];
+            }
+            const uint32_t ball = __ballot_sync(0xffffffffu, found >= 0);
+            const int srcl = ball ? __ffs(ball) - 1 : 31;
+            const int b = __shfl_sync(0xffffffffu, found >= 0 ? found : 0, srcl);
+            const int r = __shfl_sync(0xffffffffu, rem_out, srcl);
+            if (lane == 0) {
+                *sel_prefix = pfx | ((uint32_t)b << shift);
+                *sel_mask = msk | (255u << shift);
+                *need = r;
+            }
+        }
+        __syncthreads();
+    }
+}
+
 // One CTA per token.  k > 0: exact top-k (ties broken toward lower ids);
 // k == 0: logit >= threshold.  Writes labels [B][f] (1.0 / 0.0), the ascending
 // active list idx[t][0..count) (capacity `cap` per token) and counts[t].
@@ -183,15 +295,22 @@ __device__ __forceinline__ int sel_block_scan(int v, int *warp_tot, int *total) 
 // ids first) and the active ids in index order.
 __global__ void __launch_bounds__(kSelThreads)
 pred_select_kernel(const float *__restrict__ logits, int f, int k, float threshold, float *__restrict__ labels,
-                   uint32_t *__restrict__ bits, int32_t *__restrict__ idx, int cap, int32_t *__restrict__ counts) {
-    extern __shared__ uint32_t keys[];  // [f], then [kSelWarps][256] per-warp histograms
-    uint32_t *whist = keys + ((f + 3) & ~3);
-    __shared__ uint32_t hist[256];
+                   uint32_t *__restrict__ bits, int32_t *__restrict__ idx, int cap, int32_t *__restrict__ counts,
+                   const uint32_t *__restrict__ hist) {
+    // [f] keys (raw fp32 bits in threshold mode), [W] active bits, [kSelWarps][256]
+    // per-warp histograms, [f] candidate keys (top-k with the logit histogram)
+    extern __shared__ uint32_t keys[];
+    const int W = (f + 31) / 32;
+    uint32_t *sbits = keys + ((f + 3) & ~3);
+    uint32_t *whist = sbits + ((W + 3) & ~3);
+    uint32_t *cand = whist + kSelWarps * 256;
+    const bool raw = k == 0;  // threshold mode compares the fp32 logits themselves
+    pdl_enter();
+    __shared__ uint32_t bins[256];
     __shared__ uint32_t sel_prefix, sel_mask;
     __shared__ int need;
     __shared__ int warp_tot[33];
     const int t = blockIdx.x;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const float *lg = logits + (int64_t)t * f;
     if ((f & 3) == 0) {  // float4 loads, four in flight per thread
         const float4 *src = reinterpret_cast<const float4 *>(lg);
@@ -208,12 +327,15 @@ pred_select_kernel(const float *__restrict__ logits, int f, int k, float thresho
                 const int i = base + u * blockDim.x;
                 if (i < n4)
                     reinterpret_cast<uint4 *>(keys)[i] =
-                        make_uint4(order_key(v[u].x), order_key(v[u].y), order_key(v[u].z), order_key(v[u].w));
+                        raw ? make_uint4(__float_as_uint(v[u].x), __float_as_uint(v[u].y), __float_as_uint(v[u].z),
+                                         __float_as_uint(v[u].w))
+                            : make_uint4(order_key(v[u].x), order_key(v[u].y), order_key(v[u].z), order_key(v[u].w));
             }
         }
     } else {
-        for (int j = threadIdx.x; j < f; j += blockDim.x) keys[j] = order_key(lg[j]);
+        for (int j = threadIdx.x; j < f; j += blockDim.x) keys[j] = raw ? __float_as_uint(lg[j]) : order_key(lg[j]);
     }
+    for (int w = threadIdx.x; w < W; w += blockDim.x) sbits[w] = 0u;
     const bool topk = k > 0 && k < f;
     if (threadIdx.x == 0) {
         sel_prefix = 0u;
@@ -221,69 +343,48 @@ pred_select_kernel(const float *__restrict__ logits, int f, int k, float thresho
         need = k;
     }
     __syncthreads();
-    if (topk) {
-        for (int shift = 24; shift >= 0; shift -= 8) {
-            // per-warp histograms: logits crowd into a few bins, so a shared
-            // histogram would serialise the whole block on those counters
-            for (int i = threadIdx.x; i < kSelWarps * 256; i += blockDim.x) whist[i] = 0u;
-            __syncthreads();
-            const uint32_t pfx = sel_prefix, msk = sel_mask;
-            uint32_t *wh = whist + warp * 256;
-            for (int j = threadIdx.x; j < f; j += blockDim.x) {
-                const uint32_t key = keys[j];
-                if ((key & msk) == pfx) atomicAdd(&wh[(key >> shift) & 255u], 1u);
-            }
-            __syncthreads();
-            if (threadIdx.x < 256) {
-                uint32_t sum = 0;
-                for (int w = 0; w < kSelWarps; ++w) sum += whist[w * 256 + threadIdx.x];
-                hist[threadIdx.x] = sum;
-            }
-            __syncthreads();
-            if (warp == 0) {
-                // lane l holds bins 255-8l .. 248-8l (descending); the answer is
-                // the highest bin b with (count of bins > b) < need <= (count of bins >= b)
-                uint32_t c[8], sum = 0;
-#pragma unroll
-                for (int q = 0; q < 8; ++q) {
-                    c[q] = hist[255 - 8 * lane - q];
-                    sum += c[q];
-                }
-                uint32_t incl = sum;  // inclusive scan over lanes (descending bins)
-#pragma unroll
-                for (int o = 1; o < 32; o <<= 1) {
-                    const uint32_t n = __shfl_up_sync(0xffffffffu, incl, o);
-                    if (lane >= o) incl += n;
-                }
-                const int rem = need;
-                uint32_t before = incl - sum;  // keys in higher bins than this lane's
-                int found = -1, rem_out = 0;
-#pragma unroll
-                for (int q = 0; q < 8; ++q) {
-                    if (found < 0 && (int)(before + c[q]) >= rem) {
-                        found = 255 - 8 * lane - q;
-                        rem_out = rem - (int)before;
-                    }
-                    before += c[q];
-                }
-                const uint32_t ball = __ballot_sync(0xffffffffu, found >= 0);
-                const int src = ball ? __ffs(ball) - 1 : 31;
-                const int b = __shfl_sync(0xffffffffu, found >= 0 ? found : 0, src);
-                const int r = __shfl_sync(0xffffffffu, rem_out, src);
-                if (lane == 0) {
-                    sel_prefix = pfx | ((uint32_t)b << shift);
-                    sel_mask = msk | (255u << shift);
-                    need = r;
-                }
-            }
-            __syncthreads();
+    // Radix passes over `src[0..n)`: 8-bit digits at `shift`, narrowing
+    // (sel_prefix, sel_mask, need) to the key of the k-th largest element.
+    int n_src = f;
+    const uint32_t *src = keys;
+    int shift0 = 24;
+    if (topk && hist) {
+        // The logit launch counted every key's top 11 bits: the bin holding
+        // the k-th largest key and the count above it come from one scan of
+        // the 2048 bins (thread i: bins 2047 - 2i and 2046 - 2i, descending).
+        const uint32_t *h = hist + (int64_t)t * kHistBins;
+        const uint32_t ha = h[kHistBins - 1 - 2 * threadIdx.x], hb = h[kHistBins - 2 - 2 * threadIdx.x];
+        int tot0;
+        const int above = sel_block_scan((int)(ha + hb), warp_tot, &tot0);
+        if (above < k && k <= above + (int)(ha + hb)) {
+            const bool in_a = above + (int)ha >= k;
+            const uint32_t bin = in_a ? kHistBins - 1 - 2 * threadIdx.x : kHistBins - 2 - 2 * threadIdx.x;
+            sel_prefix = bin << 21;
+            sel_mask = 0xFFE00000u;
+            need = k - (in_a ? above : above + (int)ha);
         }
+        __syncthreads();
+        // Only the keys in that bin still compete: gather them (ascending
+        // index order) and finish the select on them alone.
+        const uint32_t pfx = sel_prefix;
+        const int per = (f + kSelThreads - 1) / kSelThreads;
+        const int j0 = min(f, (int)threadIdx.x * per), j1 = min(f, j0 + per);
+        int nc = 0;
+        for (int j = j0; j < j1; ++j) nc += (keys[j] & 0xFFE00000u) == pfx;
+        int ncand;
+        int pos = sel_block_scan(nc, warp_tot, &ncand);
+        for (int j = j0; j < j1; ++j)
+            if ((keys[j] & 0xFFE00000u) == pfx) cand[pos++] = keys[j];
+        __syncthreads();
+        n_src = ncand;
+        src = cand;
+        shift0 = 13;  // digits of bits 20..13, 12..5, then 7..0 (bits 7..5 already fixed)
     }
+    if (topk) radix_narrow(src, n_src, shift0, whist, bins, &sel_prefix, &sel_mask, &need);
     const uint32_t thr_key = sel_prefix;
     const int take_eq = need;  // how many keys equal to thr_key are active (lowest ids first)
-    // contiguous index run of this thread, whole 32-neuron words so that the
-    // thread writes its bit words alone
-    const int per = 32 * ((f + 32 * kSelThreads - 1) / (32 * kSelThreads));
+    // contiguous index run of this thread
+    const int per = (f + kSelThreads - 1) / kSelThreads;
     const int j0 = min(f, (int)threadIdx.x * per), j1 = min(f, j0 + per);
     int n_eq = 0;
     if (topk)
@@ -295,23 +396,22 @@ pred_select_kernel(const float *__restrict__ logits, int f, int k, float thresho
         bool active;
         if (k >= f) active = true;
         else if (k > 0) active = keys[j] > thr_key || (keys[j] == thr_key && eq_rank++ < take_eq);
-        else active = lg[j] >= threshold;  // float compare: -0.0 >= 0.0 holds
+        else active = __uint_as_float(keys[j]) >= threshold;  // float compare: -0.0 >= 0.0 holds
         n_act += active;
     }
     __syncthreads();
     int pos = sel_block_scan(n_act, warp_tot, &tot);
     eq_rank -= n_eq;  // replay the same decisions, now writing
-    const int W = (f + 31) / 32;
     uint32_t word = 0;
     for (int j = j0; j < j1; ++j) {
         bool active;
         if (k >= f) active = true;
         else if (k > 0) active = keys[j] > thr_key || (keys[j] == thr_key && eq_rank++ < take_eq);
-        else active = lg[j] >= threshold;
+        else active = __uint_as_float(keys[j]) >= threshold;
         if (labels) labels[(int64_t)t * f + j] = active ? 1.0f : 0.0f;
         word |= (active ? 1u : 0u) << (j & 31);
-        if (bits && ((j & 31) == 31 || j == j1 - 1)) {
-            bits[(int64_t)t * W + (j >> 5)] = word;
+        if ((j & 31) == 31 || j == j1 - 1) {  // runs are not word-aligned: merge in shared memory
+            if (word) atomicOr(&sbits[j >> 5], word);
             word = 0;
         }
         if (active) {
@@ -319,45 +419,202 @@ pred_select_kernel(const float *__restrict__ logits, int f, int k, float thresho
             ++pos;
         }
     }
+    if (bits) {
+        __syncthreads();
+        for (int w = threadIdx.x; w < W; w += blockDim.x) bits[(int64_t)t * W + w] = sbits[w];
+    }
     if (threadIdx.x == 0 && counts) counts[t] = tot;
+}
+
+
+// ---- grid-wide top-k for set outputs (bits / labels, no index list) --------
+// Pass A, grid (ceil(f / 256), B): every CTA finds the token's threshold bin
+// from the logit histogram, writes its 256 neurons' words (active iff the
+// key's top 11 bits are above that bin) and appends the bin's candidates.
+// Pass B, one CTA per token: exact selection among the candidates (radix
+// narrowing on the low 21 bits, equal keys taken lowest id first), whose
+// winners are ORed into the words.  The same set as pred_select_kernel.
+constexpr int kGsThreads = 256;
+
+__global__ void __launch_bounds__(kGsThreads)
+pred_gsel_a_kernel(const float *__restrict__ logits, int f, int k, const uint32_t *__restrict__ hist,
+                   uint32_t *__restrict__ bits, float *__restrict__ labels, uint2 *__restrict__ cand,
+                   uint32_t *__restrict__ cand_cnt, int2 *__restrict__ sel) {
+    __shared__ int warp_tot[kGsThreads / 32 + 1];
+    __shared__ uint32_t s_bin;
+    __shared__ int s_need;
+    pdl_enter();
+    const int t = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int W = (f + 31) / 32;
+    // thread i holds bins 2047 - 8i .. 2040 - 8i (descending)
+    const uint32_t *h = hist + (int64_t)t * kHistBins;
+    uint32_t c[8], sum = 0;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+        c[q] = h[kHistBins - 1 - 8 * tid - q];
+        sum += c[q];
+    }
+    const int incl = warp_incl_scan((int)sum);
+    if (lane == 31) warp_tot[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+        const int v = lane < kGsThreads / 32 ? warp_tot[lane] : 0;
+        const int vi = warp_incl_scan(v);
+        if (lane < kGsThreads / 32) warp_tot[lane] = vi - v;
+    }
+    __syncthreads();
+    int before = warp_tot[warp] + incl - (int)sum;  // keys in bins above this thread's
+    if (before < k && k <= before + (int)sum) {
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            if (before < k && k <= before + (int)c[q]) {
+                s_bin = kHistBins - 1 - 8 * tid - q;
+                s_need = k - before;
+            }
+            before += c[q];
+        }
+    }
+    __syncthreads();
+    const uint32_t bin = s_bin;
+    const int j = blockIdx.x * kGsThreads + tid;
+    const uint32_t key = j < f ? order_key(logits[(int64_t)t * f + j]) : 0u;
+    const bool active = j < f && (key >> 21) > bin;
+    const bool is_cand = j < f && (key >> 21) == bin;
+    const uint32_t word = __ballot_sync(0xffffffffu, active);
+    if (lane == 0 && j < f) bits[(int64_t)t * W + (j >> 5)] = word;
+    if (labels && j < f) labels[(int64_t)t * f + j] = active ? 1.0f : 0.0f;
+    const uint32_t cb = __ballot_sync(0xffffffffu, is_cand);
+    if (cb) {
+        uint32_t base = 0;
+        if (lane == 0) base = atomicAdd(cand_cnt + t, (uint32_t)__popc(cb));
+        base = __shfl_sync(0xffffffffu, base, 0);
+        if (is_cand) cand[(int64_t)t * f + base + __popc(cb & ((1u << lane) - 1u))] = make_uint2(key, (uint32_t)j);
+    }
+    if (blockIdx.x == 0 && tid == 0) sel[t] = make_int2((int)bin, s_need);
+}
+
+__global__ void __launch_bounds__(kSelThreads)
+pred_gsel_b_kernel(int f, int k, uint32_t *__restrict__ bits, float *__restrict__ labels,
+                   const uint2 *__restrict__ cand, uint32_t *__restrict__ cand_cnt, const int2 *__restrict__ sel,
+                   int32_t *__restrict__ counts) {
+    extern __shared__ uint32_t ckeys[];  // [n] candidate keys, then [kSelWarps][256] histograms
+    __shared__ uint32_t bins[256];
+    __shared__ uint32_t sel_prefix, sel_mask;
+    __shared__ int need;
+    pdl_enter();
+    const int t = blockIdx.x;
+    const int W = (f + 31) / 32;
+    const int n = (int)cand_cnt[t];
+    uint32_t *whist = ckeys + ((n + 3) & ~3);
+    const uint2 *ct = cand + (int64_t)t * f;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) ckeys[i] = ct[i].x;
+    if (threadIdx.x == 0) {
+        sel_prefix = (uint32_t)sel[t].x << 21;
+        sel_mask = 0xFFE00000u;
+        need = sel[t].y;
+    }
+    __syncthreads();
+    radix_narrow(ckeys, n, 13, whist, bins, &sel_prefix, &sel_mask, &need);
+    const uint32_t thr = sel_prefix;
+    const int take_eq = need;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const uint2 cj = ct[i];
+        bool on = cj.x > thr;
+        if (cj.x == thr) {  // equal keys: the take_eq lowest ids (candidates arrive in any order)
+            int rank = 0;
+            for (int q = 0; q < n; ++q) {
+                const uint2 o = ct[q];
+                rank += o.x == thr && o.y < cj.y;
+            }
+            on = rank < take_eq;
+        }
+        if (on) {
+            atomicOr(bits + (int64_t)t * W + (cj.y >> 5), 1u << (cj.y & 31));
+            if (labels) labels[(int64_t)t * f + cj.y] = 1.0f;
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        cand_cnt[t] = 0u;  // ready for the next call
+        if (counts) counts[t] = k;
+    }
 }
 
 int launch_predict(const __half *p1, const __half *p2, const float *x, int B, int d, int D, int f, int k,
                    float threshold, float *labels, uint32_t *bits, int32_t *idx, int32_t *counts, float *logits,
-                   __half *hidden, cudaStream_t st) {
+                   __half *hidden, const PredScratch &sc, cudaStream_t st) {
+    // logit histograms only serve the top-k selection
+    uint32_t *hist = (k > 0 && k < f) ? sc.hist : nullptr;
+    // sets without an index list: the grid-wide select
+    const bool grid_sel = hist && !idx;
     const int sms = num_sms();
-    const int ty = (B + kPredTokens - 1) / kPredTokens;
     {
+        // 8 tokens beyond B = 1: wider groups make the CUDA-core loop
+        // shared-memory and FMA bound (measured slower at B = 32 / 64)
+        const int NTH = B == 1 ? 1 : 8;
+        const int ty = (B + NTH - 1) / NTH;
         // one row per warp when that fills the GPU: every row's loads are in
         // flight at once (each warp's 8 KB row is the fixed-order dot unit)
         const int ctas = max(1, (2 * sms + ty - 1) / ty);
         const int rows = std::min((D + ctas - 1) / ctas, kPredWarps);
-        const size_t smem = sizeof(__half) * kPredTokens * d;
+        const size_t smem = sizeof(__half) * NTH * d;
         if (smem > 200 * 1024) return fail(SPB_ERR_UNSUPPORTED, "spb_predict: d too large");
-        if (int rc = ensure_smem((const void *)pred_hidden_kernel, smem)) return rc;
-        pred_hidden_kernel<<<dim3((D + rows - 1) / rows, ty), kPredThreads, smem, st>>>(p1, x, hidden, B, d, D, rows);
-        SPB_LAUNCH_CHECK("pred_hidden_kernel");
+        const bool kb16 = d / 8 >= 32 * 16;
+        auto kern = NTH == 1 ? (kb16 ? pred_hidden_kernel<1, 16> : pred_hidden_kernel<1, 8>)
+                  : NTH == 8 ? (kb16 ? pred_hidden_kernel<8, 16> : pred_hidden_kernel<8, 8>)
+                             : (kb16 ? pred_hidden_kernel<8, 16> : pred_hidden_kernel<8, 8>);
+        if (int rc = ensure_smem((const void *)kern, smem)) return rc;
+        if (int rc = launch_pdl(kern, dim3((D + rows - 1) / rows, ty), dim3(kPredThreads), smem, st,
+                                "pred_hidden_kernel", p1, x, hidden, B, d, D, rows, hist,
+                                grid_sel ? sc.cand_cnt : nullptr))
+            return rc;
     }
     {
         // at most four rows per warp: rows of D = 1024 are only 2 KB, so a
         // warp walking many of them in turn is latency-bound; more CTAs keep
-        // more rows in flight (each CTA re-stages 8 x D fp16 from L2)
+        // more rows in flight (each CTA re-stages NT x D fp16 from L2)
+        const int NTL = B == 1 ? 1 : 8;
+        const int ty = (B + NTL - 1) / NTL;
         const int ctas = max(1, (4 * sms + ty - 1) / ty);
         const int rows = std::min((f + ctas - 1) / ctas, 4 * kPredWarps);
-        const size_t smem = sizeof(__half) * kPredTokens * D;
+        const size_t smem = sizeof(__half) * NTL * D;
         if (smem > 200 * 1024) return fail(SPB_ERR_UNSUPPORTED, "spb_predict: D too large");
-        if (int rc = ensure_smem((const void *)pred_logit_kernel, smem)) return rc;
-        pred_logit_kernel<<<dim3((f + rows - 1) / rows, ty), kPredThreads, smem, st>>>(p2, hidden, logits, B, D, f,
-                                                                                       rows);
-        SPB_LAUNCH_CHECK("pred_logit_kernel");
+        auto kern = NTL == 1 ? pred_logit_kernel<1> : pred_logit_kernel<8>;
+        if (int rc = ensure_smem((const void *)kern, smem)) return rc;
+        if (int rc = launch_pdl(kern, dim3((f + rows - 1) / rows, ty), dim3(kPredThreads), smem, st,
+                                "pred_logit_kernel", p2, hidden, logits, B, D, f, rows, hist))
+            return rc;
+    }
+    if (grid_sel) {
+        uint32_t *wb = bits ? bits : sc.bits;
+        if (int rc = launch_pdl(pred_gsel_a_kernel, dim3((f + kGsThreads - 1) / kGsThreads, B), dim3(kGsThreads), 0,
+                                st, "pred_gsel_a_kernel", logits, f, k, hist, wb, labels, sc.cand, sc.cand_cnt,
+                                sc.sel))
+            return rc;
+        // candidates of the threshold bin: at most f per token
+        const size_t smem = sizeof(uint32_t) * (((f + 3) & ~3) + kSelWarps * 256);
+        if (smem > 227 * 1024) return fail(SPB_ERR_UNSUPPORTED, "spb_predict: f too large");
+        if (int rc = ensure_smem((const void *)pred_gsel_b_kernel, smem)) return rc;
+        if (int rc = launch_pdl(pred_gsel_b_kernel, dim3(B), dim3(kSelThreads), smem, st, "pred_gsel_b_kernel", f, k,
+                                wb, labels, sc.cand, sc.cand_cnt, sc.sel, counts))
+            return rc;
+        return SPB_OK;
     }
     {
-        const size_t smem = sizeof(uint32_t) * (((f + 3) & ~3) + kSelWarps * 256);
-        if (smem > 200 * 1024) return fail(SPB_ERR_UNSUPPORTED, "spb_predict: f too large");
+        // the candidate buffer doubles the key storage; without room for it
+        // the select runs its four passes over all keys
+        const size_t wpad = ((f + 31) / 32 + 3) & ~3;
+        size_t smem = sizeof(uint32_t) * (2 * ((f + 3) & ~3) + wpad + kSelWarps * 256);
+        if (smem > 227 * 1024) {
+            hist = nullptr;
+            smem = sizeof(uint32_t) * (((f + 3) & ~3) + wpad + kSelWarps * 256);
+        }
+        if (smem > 227 * 1024) return fail(SPB_ERR_UNSUPPORTED, "spb_predict: f too large");
         if (int rc = ensure_smem((const void *)pred_select_kernel, smem)) return rc;
         const int cap = k > 0 ? k : f;
-        pred_select_kernel<<<B, kSelThreads, smem, st>>>(logits, f, k, threshold, labels, bits, idx, cap, counts);
-        SPB_LAUNCH_CHECK("pred_select_kernel");
+        if (int rc = launch_pdl(pred_select_kernel, dim3(B), dim3(kSelThreads), smem, st, "pred_select_kernel",
+                                logits, f, k, threshold, labels, bits, idx, cap, counts, hist))
+            return rc;
     }
     return SPB_OK;
 }

@@ -112,8 +112,16 @@ struct DebugHooks {
 const DebugHooks &debug_hooks();
 
 // predict.cu -- low-rank activity predictor
+// predictor scratch inside the caller's workspace
+struct PredScratch {
+    uint32_t *hist;      // [B][2048] logit histograms (top 11 key bits)
+    uint2 *cand;         // [B][f] (key, id) candidates of the threshold bin
+    uint32_t *cand_cnt;  // [B]
+    int2 *sel;           // [B] threshold bin, keys still needed from it
+    uint32_t *bits;      // [B][W] set words when the caller wants labels only
+};
 int launch_predict(const __half *p1, const __half *p2, const float *x, int B, int d, int D, int f, int k,
                    float threshold, float *labels, uint32_t *bits, int32_t *idx, int32_t *counts, float *logits,
-                   __half *hidden, cudaStream_t st);
+                   __half *hidden, const PredScratch &scratch, cudaStream_t st);
 
 }  // namespace spb

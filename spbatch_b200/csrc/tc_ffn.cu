@@ -71,7 +71,7 @@ constexpr int kSlice = 256;          // output columns per down unit (two M = 12
 constexpr uint32_t kATile = 16384;   // 128 rows x 128 bytes (one 64-wide K block)
 constexpr uint32_t kDnLbo = (kDnRows / 8) * 1024;  // byte distance between 64-column blocks of a down stage
 constexpr uint32_t kDnWBytes = 4 * kDnLbo;         // 64 rows x 256 columns fp16
-constexpr int kMaxUnits = 8;          // ring units (a gate/up stage takes one or two, a down stage one)
+constexpr int kMaxUnits = 16;         // ring units (a gate/up stage takes one or two, a down stage one)
 constexpr int kMaxBufs = 16;
 constexpr uint32_t kTmemCols = 512;
 constexpr int kEpiBar = 1;           // named barrier of the epilogue warps
@@ -475,7 +475,9 @@ ffn_tc_kernel(const __grid_constant__ TcMaps maps, const TcArgs a) {
             const int rows = r1 - r0;
             const uint16_t *tids = gu_ids + r0;
             for (int st = 0; st < KG; ++st, ++s, t += GW) {
-                if (!(ok = ring_wait_empty(t, NU, ctl, a) && (GW == 1 || ring_wait_empty(t + 1, NU, ctl, a)))) break;
+                // the second unit of a two-unit stage is released by the
+                // same commit as the first
+                if (!(ok = ring_wait_empty(t, NU, ctl, a))) break;
                 const uint32_t sbase = smem_u32(ring + (size_t)(t % NU) * a.unit_bytes);
                 const int kbase = ((st + rot) % KG) * 64 * nkb;
                 if (leader) stage_stamp(a, s, 0);
@@ -532,8 +534,7 @@ ffn_tc_kernel(const __grid_constant__ TcMaps maps, const TcArgs a) {
             const int rot = KG ? clu % KG : 0;
             for (int i = 0; i < ntile && ok; ++i) {
                 for (int st = 0; st < KG; ++st, t += GW) {
-                    if (!(ok = ring_wait_empty(t, NU, ctl, a) && (GW == 1 || ring_wait_empty(t + 1, NU, ctl, a))))
-                        break;
+                    if (!(ok = ring_wait_empty(t, NU, ctl, a))) break;
                     const uint32_t sbase = smem_u32(ring + (size_t)(t % NU) * a.unit_bytes);
                     const int kbase = ((st + rot) % KG) * 64 * nkb;
                     uint64_t *bar = &ctl->tma[t % NU];
@@ -601,8 +602,12 @@ ffn_tc_kernel(const __grid_constant__ TcMaps maps, const TcArgs a) {
                 return wait_bar(&ctl->full[q % NU], par, ctl, a, kErrTimeoutFull, a.hint) &&
                        wait_bar(&ctl->tma[q % NU], par, ctl, a, kErrTimeoutFull, a.hint);
             };
-            auto wait_stage = [&](int w) -> bool {
-                if (!wait_unit(t) || (w == 2 && !wait_unit(t + 1))) return false;
+            // A two-unit stage is complete when its first unit is: the
+            // producers' arrivals there cover every copy of the stage and the
+            // TMA bytes are counted there; the second unit's barriers only
+            // keep their phase count in step.
+            auto wait_stage = [&](int) -> bool {
+                if (!wait_unit(t)) return false;
                 stage_stamp(a, s, 2);
                 // the producers' cp.async data were written through the
                 // generic proxy; make them visible to the MMA's async proxy
@@ -939,7 +944,7 @@ static size_t fixed_smem(int Np, int W, int max_gu, int max_dn) {
 }
 
 static Geometry pick_geometry(int Np, int W, int max_gu, int max_dn, int d, int force_nkb, int force_units,
-                              bool split_stages) {
+                              bool no_split) {
     const size_t fixed = fixed_smem(Np, W, max_gu, max_dn);
     const size_t budget = 227 * 1024;
     const uint32_t dn = (kDnWBytes + (uint32_t)Np * 128 + 1023) & ~1023u;
@@ -952,13 +957,13 @@ static Geometry pick_geometry(int Np, int W, int max_gu, int max_dn, int d, int 
         if (force_nkb && nkb != force_nkb) continue;
         if ((d / 64) % nkb) continue;
         const uint32_t gu = ((uint32_t)nkb * (kATile + (uint32_t)Np * 128) + 1023) & ~1023u;
-        // Splitting a gate/up stage over two units lets more down stages fly,
-        // but the extra barrier waits in the MMA issue loop cost more than
-        // that gains (measured): one unit per stage unless asked otherwise.
-        uint32_t unit = gu > dn ? gu : dn;
-        if (split_stages) unit = dn > (gu + 1) / 2 ? dn : (((gu + 1) / 2 + 1023) & ~1023u);
-        const int gw = gu > unit ? 2 : 1;
-        if (gw == 1) unit = gu > dn ? gu : dn;
+        // When two down stages fit in one gate/up stage, the ring counts
+        // half-stage units: a gate/up stage takes two, a down stage one, so
+        // twice as many down stages are in flight (and prefetched while the
+        // gate/up phase ends).
+        const bool halves = !no_split && 2 * dn <= gu;
+        const uint32_t unit = halves ? gu / 2 : (gu > dn ? gu : dn);
+        const int gw = halves ? 2 : 1;
         if (budget < fixed + 2u * gw * unit) continue;
         int nu = (int)std::min<size_t>((budget - fixed) / unit, kMaxUnits);
         if (force_units) nu = std::min(nu, force_units);
@@ -1054,7 +1059,7 @@ int launch_ffn_tc(const TcLaunch &L, cudaStream_t st) {
         a.KC = std::max(1, (2 * nclu) / MT);
         a.max_gu = (L.f + nclu - 1) / nclu + 1;
         a.max_dn = (L.f + a.KC - 1) / a.KC + 128;
-        g = pick_geometry(Np, a.W, a.max_gu, a.max_dn, L.d, dbg.nkb, dbg.stages, dbg.split_stages != 0);
+        g = pick_geometry(Np, a.W, a.max_gu, a.max_dn, L.d, dbg.nkb, dbg.stages, dbg.split_stages != 0);  // test hook: 1 = whole-stage units
         if (g.nu < 2) return fail(SPB_ERR_UNSUPPORTED, "tensor path: shared memory too small for two stages");
         if ((rc = ensure_smem((const void *)ffn_tc_kernel, g.smem))) return rc;
         const int fit = max_clusters(g.smem, sms);

@@ -46,7 +46,7 @@ def _run(spb, cuda, p1, p2, x, k, thr=0.0):
 
 
 @pytest.mark.parametrize("B,d,D,f,k", [(1, 4096, 1024, 11008, 1101), (4, 512, 256, 1000, 100), (19, 1024, 512, 2048, 300),
-                                       (64, 5120, 1024, 13824, 1106)])
+                                       (64, 5120, 1024, 13824, 1106), (2, 8192, 1024, 28672, 2867)])
 def test_predict_bit_exact(spb, cuda, oracle_mod, B, d, D, f, k):
     rng = np.random.default_rng(B * 7 + f)
     p1, p2 = _weights(rng, d, D, f)
@@ -95,3 +95,37 @@ def test_predict_then_ffn_config1(spb, cuda, oracle_mod):
     _, lab_ref, _, _ = oracle_mod.predict(p1, p2, x, k=k)
     np.testing.assert_array_equal(labels.cpu().numpy(), lab_ref)
     assert_close(out.cpu().numpy(), oracle_mod.ffn(*W, x, lab_ref))
+
+
+def _to_words(lab):
+    b = np.packbits((lab > 0).astype(np.uint8), axis=1, bitorder="little")
+    return np.pad(b, ((0, 0), (0, (-b.shape[1]) % 4))).view(np.uint32)
+
+
+@pytest.mark.parametrize("B,d,D,f,k,ties", [(1, 4096, 1024, 11008, 1101, False), (5, 512, 256, 1000, 100, False),
+                                            (2, 512, 256, 512, 37, True), (64, 5120, 1024, 13824, 1106, False),
+                                            (2, 8192, 1024, 28672, 2867, False)])
+def test_grid_select_sets_bit_exact(spb, cuda, oracle_mod, B, d, D, f, k, ties):
+    """Set outputs without an index list take the grid-wide select (threshold
+    bin from the logit histogram, exact selection among its candidates):
+    labels and bit words bit-exact against the oracle, ties included, on two
+    calls in a row (the candidate counters reset themselves)."""
+    import torch
+    rng = np.random.default_rng(B * 11 + f)
+    p1, p2 = _weights(rng, d, D, f)
+    if ties:
+        p2[100:200] = p2[5]  # 100 neurons share one logit per token
+    P1, P2 = _dev(p1, cuda), _dev(p2, cuda)
+    ws = spb.predict_workspace(B, D, f, cuda)
+    for call in range(2):
+        x = rng.standard_normal((B, d)).astype(np.float32)
+        X = _dev(x, cuda)
+        _, lab_ref, _, cnt_ref = oracle_mod.predict(p1, p2, x, k=k)
+        bits = torch.zeros((B, (f + 31) // 32), dtype=torch.int32, device=cuda)
+        labels = spb.predict(P1, P2, X, k=k, bits_out=bits, workspace=ws)
+        bits_only = torch.zeros_like(bits)
+        spb.predict(P1, P2, X, k=k, bits_out=bits_only, labels=False, workspace=ws)
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(labels.cpu().numpy(), lab_ref, err_msg=f"labels, call {call}")
+        np.testing.assert_array_equal(bits.cpu().numpy().view(np.uint32), _to_words(lab_ref), err_msg="bits")
+        np.testing.assert_array_equal(bits_only.cpu().numpy().view(np.uint32), _to_words(lab_ref), err_msg="bits")
