@@ -8,7 +8,11 @@
  * caller-owned device workspace whose size spb_ffn_workspace_bytes() reports.
  * The first 4 bytes of a workspace hold a sticky device error code (0 = no
  * error): kernels whose bounded waits run out record a code there and return
- * instead of hanging the GPU; only the caller clears it.
+ * instead of hanging the GPU; only the caller clears it.  Codes of the
+ * tensor-core kernel: 1 a stage's copies never landed, 2 a stage was never
+ * released, 3 accumulator hand-off, 4 the partner CTA's results never
+ * arrived, 5 a cluster never published its h rows, 6 the grid barrier, 7 the
+ * kernel was launched without its 2-CTA clusters (nothing was computed).
  *
  * Each entry point names the reference interface it replaces
  * (cuda/kernel.cuh / cuda/kernel.cu of SMAC-Zhang/SpBatch).  The reference's
@@ -119,6 +123,20 @@ int spb_ffn_forward_bits(const void *w_gate, const void *w_up, const void *w_dow
                          const uint32_t *tok_bits, int B, int d, int f, int act, int per_token_mask, int path,
                          float *out, int32_t *merge_idx_out, int32_t *count_out, void *workspace,
                          size_t workspace_bytes, void *stream);
+
+/*
+ * spb_ffn_forward with the linear layers' biases: bias_gate / bias_up [f]
+ * fp16 (either nullable) are added, in fp32, to each active neuron's gate /
+ * up product before the activation -- the sparse bias add of add_sparse_cuda
+ * (cuda/kernel.cuh:128, cuda/kernel.cu:818-830, 1055-1063), fused into every
+ * path's epilogue instead of a separate pass over the compacted [B][f]
+ * products.  The sets come as labels (idx) or bit words (tok_bits): exactly
+ * one of the two.
+ */
+int spb_ffn_forward_bias(const void *w_gate, const void *w_up, const void *w_down, int wtype, const float *x,
+                         const float *idx, const uint32_t *tok_bits, const void *bias_gate, const void *bias_up, int B,
+                         int d, int f, int act, int per_token_mask, int path, float *out, int32_t *merge_idx_out,
+                         int32_t *count_out, void *workspace, size_t workspace_bytes, void *stream);
 
 /*
  * Block-quantised weights (BASELINE: ggml Q8_0 / Q4_0; the reference has only

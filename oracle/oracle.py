@@ -62,6 +62,7 @@ def lib():
         _lib.spbo_up_compact.argtypes = [P, P, P, P, i, i, i, i, i, P]
         _lib.spbo_down_compact.argtypes = [P, P, P, P, i, i, i, i, i, P]
         _lib.spbo_ffn.argtypes = [P, P, P, P, P, i, i, i, i, i, i, P]
+        _lib.spbo_ffn_bias.argtypes = [P, P, P, P, P, P, P, i, i, i, i, i, i, P]
         _lib.spbo_ffn_f32w.argtypes = [P, P, P, P, P, i, i, i, i, i, i, P]
         _lib.spbo_round_f16.argtypes = [P, P, C.c_int64]
         _lib.spbo_f32_to_f16_array.argtypes = [P, P, C.c_int64]
@@ -147,6 +148,20 @@ def ffn(wg, wu, wd, x, idx, G=None, per_token=True, act=0):
     G = B if G is None else G
     out = np.zeros((B, d), np.float32)
     lib().spbo_ffn(_p(wg), _p(wu), _p(wd), _p(x), _p(idx), B, d, f, G, int(per_token), act, _p(out))
+    return out
+
+
+def ffn_bias(wg, wu, wd, x, idx, bias_gate=None, bias_up=None, per_token=True, act=0):
+    """ffn with fp16 neuron biases (either None) added to gate / up before the activation."""
+    wg, wu, wd = _u16(wg), _u16(wu), _u16(wd)
+    x, idx = _f32(x), _f32(idx)
+    B, d = x.shape
+    f = wg.shape[0]
+    bg = None if bias_gate is None else _u16(bias_gate)
+    bu = None if bias_up is None else _u16(bias_up)
+    out = np.zeros((B, d), np.float32)
+    lib().spbo_ffn_bias(_p(wg), _p(wu), _p(wd), _p(x), _p(idx), None if bg is None else _p(bg),
+                        None if bu is None else _p(bu), B, d, f, B, int(per_token), act, _p(out))
     return out
 
 

@@ -191,8 +191,19 @@ void spbo_down_compact(const uint16_t *wd, const float *h, const int32_t *merge_
  * x is rounded to fp16 before gate/up; h is rounded to fp16 before down.
  * out is [B][d] fp32.
  */
+/* spbo_ffn with neuron biases bg / bu (fp16 [f], nullable) added to the fp32
+ * gate / up products before the activation, as add_sparse_cuda adds them
+ * (cuda/kernel.cu:818-830: c = a + (float)b[merge_idx[row]]). */
+void spbo_ffn_bias(const uint16_t *wg, const uint16_t *wu, const uint16_t *wd, const float *x, const float *idx,
+                   const uint16_t *bg, const uint16_t *bu, int B, int d, int f, int G, int mode, int act, float *out);
+
 void spbo_ffn(const uint16_t *wg, const uint16_t *wu, const uint16_t *wd, const float *x, const float *idx,
               int B, int d, int f, int G, int mode, int act, float *out) {
+    spbo_ffn_bias(wg, wu, wd, x, idx, NULL, NULL, B, d, f, G, mode, act, out);
+}
+
+void spbo_ffn_bias(const uint16_t *wg, const uint16_t *wu, const uint16_t *wd, const float *x, const float *idx,
+                   const uint16_t *bg, const uint16_t *bu, int B, int d, int f, int G, int mode, int act, float *out) {
     int S = (B + G - 1) / G;
     int32_t *merge = (int32_t *)malloc(sizeof(int32_t) * (size_t)S * f);
     int32_t *counts = (int32_t *)malloc(sizeof(int32_t) * S);
@@ -214,6 +225,8 @@ void spbo_ffn(const uint16_t *wg, const uint16_t *wu, const uint16_t *wd, const 
                 u += (double)spbo_f16_to_f32(ru[k]) * (double)xr[k];
             }
             float gf = (float)g, uf = (float)u;
+            if (bg) gf += spbo_f16_to_f32(bg[j]);
+            if (bu) uf += spbo_f16_to_f32(bu[j]);
             float hf = (gf > 0.0f ? gf : 0.0f) * (act == 1 ? (uf > 0.0f ? uf : 0.0f) : uf);
             hf = r16(hf);
             if (hf == 0.0f) continue;

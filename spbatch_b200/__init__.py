@@ -72,6 +72,7 @@ def _bind(L: C.CDLL) -> None:
     L.spb_predict_workspace_bytes.restype = Z
     L.spb_predict.argtypes = [P, P, P, I, I, I, I, I, C.c_float, P, P, P, P, P, P, Z, P]
     L.spb_ffn_forward_bits.argtypes = [P, P, P, I, P, P, I, I, I, I, I, I, P, P, P, P, Z, P]
+    L.spb_ffn_forward_bias.argtypes = [P, P, P, I, P, P, P, P, P, I, I, I, I, I, I, P, P, P, P, Z, P]
     L.spb_ffn_forward.argtypes = [P, P, P, I, P, P, I, I, I, I, I, I, P, P, P, P, Z, P]
     L.spb_ffn_launches.argtypes = [I, I, I, I]
     L.spb_trace_enable.argtypes = [P, Z]
@@ -144,18 +145,21 @@ def union(idx, group: int = 0, workspace=None, stream=None):
 
 def ffn_forward(w_gate, w_up, w_down, x, idx=None, *, bits=None, f: int | None = None, wtype: int = W_F16,
                 act: int = ACT_RELU_MUL, per_token_mask: bool = True, path: int = PATH_AUTO, out=None,
-                workspace=None, merge_idx_out=None, count_out=None, stream=None, check: bool = False):
+                workspace=None, merge_idx_out=None, count_out=None, stream=None, check: bool = False,
+                bias_gate=None, bias_up=None):
     """One sparse FFN layer on the GPU (see spb_ffn_forward in include/spb.h).
 
     w_gate / w_up / w_down: [f][d] rows (W_down stored transposed, as the
     reference stores it); x [B][d] fp32; the active sets either as idx [B][f]
     fp32 labels (> 0 active) or as bits [B][ceil(f/32)] int32 words
     (spb_ffn_forward_bits; f is then w_gate's row count unless given).
+    bias_gate / bias_up ([f] fp16) add the linear layers' biases to the gate
+    / up products before the activation (spb_ffn_forward_bias).
     check=True waits for the layer and raises if a bounded device wait ran
     out (the workspace's error word, which it then clears).
     """
     import torch
-    _require_cuda(w_gate, w_up, w_down, x, idx, bits, out, merge_idx_out, count_out)
+    _require_cuda(w_gate, w_up, w_down, x, idx, bits, out, merge_idx_out, count_out, bias_gate, bias_up)
     if (idx is None) == (bits is None):
         raise SpbError("ffn_forward: give exactly one of idx (labels) and bits")
     B, d = x.shape
@@ -166,10 +170,17 @@ def ffn_forward(w_gate, w_up, w_down, x, idx=None, *, bits=None, f: int | None =
     if out is None:
         out = torch.empty((B, d), dtype=torch.float32, device=x.device)
     ws = workspace if workspace is not None else new_workspace(B, d, f, 0, x.device)
-    fn, sets = (lib().spb_ffn_forward, idx) if idx is not None else (lib().spb_ffn_forward_bits, bits)
-    _check(fn(w_gate.data_ptr(), w_up.data_ptr(), w_down.data_ptr(), wtype, x.data_ptr(), sets.data_ptr(), B, d, f,
-              act, int(per_token_mask), path, out.data_ptr(), _ptr(merge_idx_out), _ptr(count_out), ws.data_ptr(),
-              ws.numel(), _stream(stream)), "spb_ffn_forward")
+    if bias_gate is not None or bias_up is not None:
+        _check(lib().spb_ffn_forward_bias(w_gate.data_ptr(), w_up.data_ptr(), w_down.data_ptr(), wtype, x.data_ptr(),
+                                          _ptr(idx), _ptr(bits), _ptr(bias_gate), _ptr(bias_up), B, d, f, act,
+                                          int(per_token_mask), path, out.data_ptr(), _ptr(merge_idx_out),
+                                          _ptr(count_out), ws.data_ptr(), ws.numel(), _stream(stream)),
+               "spb_ffn_forward_bias")
+    else:
+        fn, sets = (lib().spb_ffn_forward, idx) if idx is not None else (lib().spb_ffn_forward_bits, bits)
+        _check(fn(w_gate.data_ptr(), w_up.data_ptr(), w_down.data_ptr(), wtype, x.data_ptr(), sets.data_ptr(), B, d,
+                  f, act, int(per_token_mask), path, out.data_ptr(), _ptr(merge_idx_out), _ptr(count_out),
+                  ws.data_ptr(), ws.numel(), _stream(stream)), "spb_ffn_forward")
     if check:
         code = device_error(ws)
         if code:

@@ -111,9 +111,10 @@ int spb_union(const float *idx, int B, int f, int group, int32_t *merge_idx, int
 // The layer with the active sets either as fp32 labels (idx) or as per-token
 // bit words (tok_in); exactly one of the two is given.
 static int ffn_impl(const void *w_gate, const void *w_up, const void *w_down, int wtype, const float *x,
-                    const float *idx, const uint32_t *tok_in, int B, int d, int f, int act, int per_token_mask,
-                    int path, float *out, int32_t *merge_idx_out, int32_t *count_out, void *workspace,
-                    size_t workspace_bytes, void *stream) {
+                    const float *idx, const uint32_t *tok_in, const void *bias_gate, const void *bias_up, int B,
+                    int d, int f, int act, int per_token_mask, int path, float *out, int32_t *merge_idx_out,
+                    int32_t *count_out, void *workspace, size_t workspace_bytes, void *stream) {
+    const __half *bg = static_cast<const __half *>(bias_gate), *bu = static_cast<const __half *>(bias_up);
     if (!w_gate || !w_up || !w_down || !x || (!idx && !tok_in) || !out)
         return fail(SPB_ERR_INVALID, "spb_ffn_forward: null pointer");
     if (B <= 0 || d <= 0 || f <= 0) return fail(SPB_ERR_INVALID, "spb_ffn_forward: bad shape");
@@ -148,6 +149,8 @@ static int ffn_impl(const void *w_gate, const void *w_up, const void *w_down, in
         L.wd = w_down;
         L.labels = idx;
         L.tok_in = tok_in;
+        L.bias_g = bg;
+        L.bias_u = bu;
         L.x = x;
         L.gbar = ws.gbar;
         L.x16 = ws.x16;
@@ -181,6 +184,8 @@ static int ffn_impl(const void *w_gate, const void *w_up, const void *w_down, in
         sa.x = x;
         sa.idx = idx;
         sa.tok_in = tok_in;
+        sa.bias_g = bg;
+        sa.bias_u = bu;
         sa.B = B;
         sa.d = d;
         sa.f = f;
@@ -214,6 +219,8 @@ static int ffn_impl(const void *w_gate, const void *w_up, const void *w_down, in
             sa.x = x + (int64_t)t0 * d;
             sa.idx = idx ? idx + (int64_t)t0 * f : nullptr;
             sa.tok_in = tok_in ? tok_in + (int64_t)t0 * words_of(f) : nullptr;
+            sa.bias_g = bg;
+            sa.bias_u = bu;
             sa.B = B - t0 < chunk ? B - t0 : chunk;
             sa.d = d;
             sa.f = f;
@@ -247,6 +254,8 @@ static int ffn_impl(const void *w_gate, const void *w_up, const void *w_down, in
     a.f = f;
     a.seg_bits = ws.seg_bits;
     a.tok_bits = tok_in ? tok_in : ws.tok_bits;
+    a.bias_g = bg;
+    a.bias_u = bu;
     a.act = act;
     a.per_token = per_token_mask;
     a.h = ws.h;
@@ -264,8 +273,8 @@ int spb_ffn_forward(const void *w_gate, const void *w_up, const void *w_down, in
                     int32_t *merge_idx_out, int32_t *count_out, void *workspace, size_t workspace_bytes,
                     void *stream) {
     if (!idx) return fail(SPB_ERR_INVALID, "spb_ffn_forward: null pointer");
-    return ffn_impl(w_gate, w_up, w_down, wtype, x, idx, nullptr, B, d, f, act, per_token_mask, path, out,
-                    merge_idx_out, count_out, workspace, workspace_bytes, stream);
+    return ffn_impl(w_gate, w_up, w_down, wtype, x, idx, nullptr, nullptr, nullptr, B, d, f, act, per_token_mask,
+                    path, out, merge_idx_out, count_out, workspace, workspace_bytes, stream);
 }
 
 int spb_ffn_forward_bits(const void *w_gate, const void *w_up, const void *w_down, int wtype, const float *x,
@@ -273,8 +282,20 @@ int spb_ffn_forward_bits(const void *w_gate, const void *w_up, const void *w_dow
                          float *out, int32_t *merge_idx_out, int32_t *count_out, void *workspace,
                          size_t workspace_bytes, void *stream) {
     if (!tok_bits) return fail(SPB_ERR_INVALID, "spb_ffn_forward_bits: null pointer");
-    return ffn_impl(w_gate, w_up, w_down, wtype, x, nullptr, tok_bits, B, d, f, act, per_token_mask, path, out,
-                    merge_idx_out, count_out, workspace, workspace_bytes, stream);
+    return ffn_impl(w_gate, w_up, w_down, wtype, x, nullptr, tok_bits, nullptr, nullptr, B, d, f, act,
+                    per_token_mask, path, out, merge_idx_out, count_out, workspace, workspace_bytes, stream);
+}
+
+int spb_ffn_forward_bias(const void *w_gate, const void *w_up, const void *w_down, int wtype, const float *x,
+                         const float *idx, const uint32_t *tok_bits, const void *bias_gate, const void *bias_up, int B,
+                         int d, int f, int act, int per_token_mask, int path, float *out, int32_t *merge_idx_out,
+                         int32_t *count_out, void *workspace, size_t workspace_bytes, void *stream) {
+    if ((idx == nullptr) == (tok_bits == nullptr))
+        return fail(SPB_ERR_INVALID, "spb_ffn_forward_bias: give exactly one of idx and tok_bits");
+    if ((bias_gate && ((uintptr_t)bias_gate & 1)) || (bias_up && ((uintptr_t)bias_up & 1)))
+        return fail(SPB_ERR_INVALID, "spb_ffn_forward_bias: biases must be 2-byte aligned fp16");
+    return ffn_impl(w_gate, w_up, w_down, wtype, x, idx, tok_bits, bias_gate, bias_up, B, d, f, act, per_token_mask,
+                    path, out, merge_idx_out, count_out, workspace, workspace_bytes, stream);
 }
 
 // Predictor workspace: fp16 hidden [B][D], fp32 logits [B][f], then the

@@ -204,7 +204,12 @@ __global__ void __launch_bounds__(kGemvThreads) fused_gateup_gemv_kernel(FusedGe
 #pragma unroll
                 for (int t = 0; t < NT; ++t) {
                     if (t < nt) {
-                        float hv = apply_act(ag[t], au[t], a.act);
+                        // sparse bias add (cuda/kernel.cu:818-830): fp16 bias
+                        // of the neuron added to the fp32 product
+                        float gv = ag[t], uv = au[t];
+                        if (a.bias_g) gv += __half2float(a.bias_g[j]);
+                        if (a.bias_u) uv += __half2float(a.bias_u[j]);
+                        float hv = apply_act(gv, uv, a.act);
                         if (a.per_token) {
                             const uint32_t word = a.tok_bits[(int64_t)(t0 + t) * W + (j >> 5)];
                             if (!((word >> (j & 31)) & 1u)) hv = 0.0f;

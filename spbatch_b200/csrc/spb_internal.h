@@ -36,6 +36,7 @@ struct FusedGemvArgs {
     int B, d, f;
     const uint32_t *seg_bits;   // [W] batch union
     const uint32_t *tok_bits;   // [B][W]
+    const __half *bias_g, *bias_u;  // [f] fp16 gate / up biases, or null
     int act, per_token;
     __half *h;                  // [f][B] compacted
     int32_t *merge;             // [f] out: union ids
@@ -53,6 +54,7 @@ struct StreamFfnArgs {
     const float *x;            // [B][d]
     const float *idx;          // [B][f] labels, active if > 0 (or null with tok_in)
     const uint32_t *tok_in;    // [B][W] per-token activity bits, or null
+    const __half *bias_g, *bias_u;  // [f] fp16 gate / up biases, or null
     int B, d, f, act, per_token;
     int32_t *merge_out;        // [f] optional: ascending union ids
     int32_t *count_out;        // [1] optional: union size
@@ -92,7 +94,8 @@ struct TcLaunch {
     int32_t *merge_out, *count_out;
     float *xchg;              // [grid][Np][64] partner-exchange slots
     uint32_t *ready;          // [grid / 2] per-cluster counters
-    unsigned int *gbar;       // [2] grid barrier (count, generation), zero when first used
+    unsigned int *gbar;       // [3] per-launch counters, zero when first used
+    const __half *bias_g, *bias_u;  // [f] fp16 gate / up biases, or null
     uint32_t *err;
     int B, Np, d, f, fpad, act, per_token, grid;
 };

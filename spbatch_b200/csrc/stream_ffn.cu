@@ -76,6 +76,7 @@ struct SfArgs {
     const float *x;               // [B][d]
     const float *idx;             // [B][f] labels, or null with tok_in
     const uint32_t *tok_in;       // [B][W] per-token activity bits, or null
+    const __half *bias_g, *bias_u;  // [f] fp16 gate / up biases, or null
     float *out;                   // [B][d]
     int32_t *merge;               // [f] or null
     int32_t *count;               // [1] or null
@@ -575,8 +576,15 @@ __global__ void __launch_bounds__(kSfThreads, 1) stream_ffn_kernel(const SfArgs 
             // lanes v < G*NT hold gate sums; the matching up sum is in lane v + G*NT
             const float up = __shfl_sync(0xffffffffu, tot, (lane + G * NT) & 31);
             uint32_t hbits = 0;  // fp16 h of (neuron lane / NT, token lane % NT)
-            if (lane < G * NT && ((hmask >> lane) & 1u))
-                hbits = __half_as_ushort(__float2half_rn(sf_act(tot, up, a.act)));
+            if (lane < G * NT && ((hmask >> lane) & 1u)) {
+                float gs = tot, us = up;
+                if (a.bias_g || a.bias_u) {  // sparse bias add (cuda/kernel.cu:818-830)
+                    const int jn = nid[i0 + lane / NT];
+                    if (a.bias_g) gs += __half2float(a.bias_g[jn]);
+                    if (a.bias_u) us += __half2float(a.bias_u[jn]);
+                }
+                hbits = __half_as_ushort(__float2half_rn(sf_act(gs, us, a.act)));
+            }
 #pragma unroll
             for (int g = 0; g < G; ++g) {
                 uint32_t h[NT];
@@ -665,6 +673,8 @@ int launch_sf(const StreamFfnArgs &fa, cudaStream_t st) {
     a.x = fa.x;
     a.idx = fa.idx;
     a.tok_in = fa.tok_in;
+    a.bias_g = fa.bias_g;
+    a.bias_u = fa.bias_u;
     a.out = fa.out;
     a.merge = fa.merge_out;
     a.count = fa.count_out;

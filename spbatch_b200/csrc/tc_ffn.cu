@@ -84,6 +84,7 @@ enum : uint32_t {
     kErrTimeoutXchg = 4,   // the partner CTA's gate/up results never arrived
     kErrTimeoutFlag = 5,   // down phase: a cluster never published its h
     kErrTimeoutGrid = 6,   // the grid barrier after the union never completed
+    kErrLaunchShape = 7,   // launched without 2-CTA clusters or with an odd grid
 };
 
 struct TcCtl {
@@ -109,6 +110,7 @@ struct TcArgs {
     __half *x16;                 // [Np][d] fp16 activations (rows >= B zero), written in phase 0
     __half *h16;                 // [Np][fpad] h, K-major per token
     uint32_t *seg_bits;          // [W] batch union, written in phase 0
+    const __half *bias_g, *bias_u;  // [f] fp16 gate / up biases, or null
     unsigned int *gbar;          // [3] per-launch counters: grid-barrier arrivals, CTAs whose share of
                                  // the activations / zeroed output is written, CTAs done (zero on entry;
                                  // the last CTA to finish resets them and the cluster counters)
@@ -312,6 +314,14 @@ ffn_tc_kernel(const __grid_constant__ TcMaps maps, const TcArgs a) {
     uint32_t *bits = reinterpret_cast<uint32_t *>(wtot + 64);                // [W]
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    // The pairing, the exchange through the partner's shared memory and the
+    // grid-wide counters assume 2-CTA clusters over an even grid; a launch
+    // that arrives in any other shape (a tool that replays it without its
+    // cluster attribute) records an error and touches nothing else.
+    if (cluster_nctarank() != 2u || (gridDim.x & 1u)) {
+        if (tid == 0) atomicCAS(a.err, 0u, (uint32_t)kErrLaunchShape);
+        return;
+    }
     const uint32_t rank = cluster_ctarank(), peer = rank ^ 1u;
     const int clu = blockIdx.x >> 1, nclu = gridDim.x >> 1;
 
@@ -760,6 +770,8 @@ ffn_tc_kernel(const __grid_constant__ TcMaps maps, const TcArgs a) {
             const int pos = P0 + r0 + e;
             if (mine_half) {
                 __half *hcol = a.h16 + pos;
+                const float bgj = (a.bias_g && valid) ? __half2float(a.bias_g[j]) : 0.0f;
+                const float buj = (a.bias_u && valid) ? __half2float(a.bias_u[j]) : 0.0f;
                 for (int c0 = 0; c0 < Np; c0 += 16) {
                     float mine[16];
                     tmem_ld16(acc + c0, mine);
@@ -777,8 +789,9 @@ ffn_tc_kernel(const __grid_constant__ TcMaps maps, const TcArgs a) {
 #pragma unroll
                         for (int q = 0; q < 16; ++q) {
                             const int t = c0 + q;
-                            const float g = rank ? other[q] : mine[q];
-                            const float u = rank ? mine[q] : other[q];
+                            // sparse bias add (cuda/kernel.cu:818-830) before the activation
+                            const float g = (rank ? other[q] : mine[q]) + bgj;
+                            const float u = (rank ? mine[q] : other[q]) + buj;
                             float hv = 0.0f;
                             if (t < a.B && ((mw >> q) & 1u)) hv = act_h(g, u, a.act);
                             hcol[(int64_t)t * a.fpad] = __float2half_rn(hv);
@@ -1024,6 +1037,8 @@ int launch_ffn_tc(const TcLaunch &L, cudaStream_t st) {
     a.x = L.x;
     a.x16 = L.x16;
     a.gbar = L.gbar;
+    a.bias_g = L.bias_g;
+    a.bias_u = L.bias_u;
     a.h16 = L.h16;
     a.seg_bits = L.seg_bits;
     a.out = L.out;

@@ -183,6 +183,12 @@ __device__ __forceinline__ uint32_t cluster_ctarank() {
     return r;
 }
 
+__device__ __forceinline__ uint32_t cluster_nctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
+    return r;
+}
+
 // Address of the same shared-memory location in cluster CTA `rank`.
 __device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
     uint32_t r;

@@ -379,3 +379,31 @@ def test_bits_input_matches_labels(spb, cuda, oracle_mod, B, d, f, path):
     want = oracle_mod.ffn(*W, x, lab)
     (assert_close_70b if d >= 8192 else assert_close)(outs[0], want)
     (assert_close_70b if d >= 8192 else assert_close)(outs[1], want)
+
+
+@pytest.mark.parametrize("B,d,f,path,which", [(1, 4096, 11008, 1, "both"), (3, 1024, 2050, 1, "gate"),
+                                              (6, 1024, 2050, 1, "up"), (8, 1024, 4096, 2, "both"),
+                                              (32, 4096, 11008, 2, "both"), (64, 1024, 4096, 2, "gate")])
+def test_bias_in_fused_epilogues(spb, cuda, oracle_mod, B, d, f, path, which):
+    """Sparse bias add (add_sparse_cuda, cuda/kernel.cu:818-830) fused into
+    every path: streaming (B <= 4), token groups / fallback GEMV (B = 6 with
+    the index outputs requested), tensor cores; labels and bit-word input."""
+    import torch
+    rng = np.random.default_rng(3000 + B + f)
+    W = _layer(rng, d, f, 0.02 if d >= 4096 else 0.04)
+    x = rng.standard_normal((B, d)).astype(np.float32)
+    lab = zipf_active_labels(B, f, max(1, f // 10), seed=7 * B)
+    bg = (rng.standard_normal(f) * 0.5).astype(np.float16) if which in ("both", "gate") else None
+    bu = (rng.standard_normal(f) * 0.5).astype(np.float16) if which in ("both", "up") else None
+    want = oracle_mod.ffn_bias(*W, x, lab, bg, bu)
+    Wd = [_dev(w, cuda) for w in W]
+    for sets in ("labels", "bits"):
+        ws = spb.new_workspace(B, d, f, 0, cuda)
+        kw = dict(idx=_dev(lab, cuda)) if sets == "labels" else dict(bits=_dev(_to_bits(lab), cuda))
+        merge = torch.empty(f, dtype=torch.int32, device=cuda) if B == 6 else None  # B = 6: the fallback GEMV
+        out = spb.ffn_forward(*Wd, _dev(x, cuda), **kw, path=path, workspace=ws, merge_idx_out=merge,
+                              bias_gate=None if bg is None else _dev(bg, cuda),
+                              bias_up=None if bu is None else _dev(bu, cuda))
+        torch.cuda.synchronize()
+        assert _ws_error(ws) == 0
+        assert_close(out.cpu().numpy(), want)

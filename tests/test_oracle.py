@@ -147,3 +147,22 @@ def test_predictor_oracle_vs_numpy(oracle_mod):
     _, lab0, _, c0 = oracle_mod.predict(p1, p2, x, k=0, threshold=0.0)
     np.testing.assert_array_equal(lab0, (lg >= 0).astype(np.float32))
     assert (c0 == lab0.sum(1)).all()
+
+
+def test_oracle_bias_reduces_to_plain_ffn(oracle_mod):
+    """With zero biases the biased oracle is the plain one; with a gate bias it
+    matches a numpy restatement of add-then-activate."""
+    rng = np.random.default_rng(5)
+    B, d, f = 3, 64, 96
+    W = [(rng.standard_normal((f, d)) * 0.1).astype(np.float16) for _ in range(3)]
+    x = rng.standard_normal((B, d)).astype(np.float32)
+    lab = (rng.random((B, f)) < 0.3).astype(np.float32)
+    z = np.zeros(f, np.float16)
+    np.testing.assert_array_equal(oracle_mod.ffn_bias(*W, x, lab, z, z), oracle_mod.ffn(*W, x, lab))
+    bg = (rng.standard_normal(f) * 0.5).astype(np.float16)
+    xr = x.astype(np.float16).astype(np.float64)
+    g = (xr @ W[0].astype(np.float64).T).astype(np.float32) + bg.astype(np.float32)
+    u = (xr @ W[1].astype(np.float64).T).astype(np.float32)
+    h = (np.maximum(g, 0) * u * (lab > 0)).astype(np.float16).astype(np.float64)
+    want = h @ W[2].astype(np.float64)
+    np.testing.assert_allclose(oracle_mod.ffn_bias(*W, x, lab, bg, None), want, rtol=1e-5, atol=1e-5)

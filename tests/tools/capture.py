@@ -84,7 +84,8 @@ def main(argv):
             gate_up(wg.data_ptr(), wu.data_ptr(), x.data_ptr(), dst[0].data_ptr(), dst[1].data_ptr(), merge.data_ptr(),
                     M, N, K, act.data_ptr(), st, st)
             relu_mul(dst[0].data_ptr(), dst[1].data_ptr(), dst[3].data_ptr(), M, N, st)
-            down(wd.data_ptr(), dst[3].data_ptr(), outd.data_ptr(), merge.data_ptr(), K, M, N, act.data_ptr(), st)
+            # cuda/ffn_test.cu: down_mul_mat_cuda_sparse(w, h, out, merge, K = d, M = batch, N = f, ...)
+            down(wd.data_ptr(), dst[3].data_ptr(), outd.data_ptr(), merge.data_ptr(), K, N, M, act.data_ptr(), st)
     elif kind == "dequant":
         rb = int(spb.lib().spb_weight_row_bytes(spb.W_Q4_0, d))
         q = torch.randint(0, 255, (f, rb), dtype=torch.uint8, device=dev)
