@@ -26,6 +26,10 @@ enum {
     SPB_DEBUG_TC_HINT_ACC = 5, /* tensor path: suspend hint of the epilogue's accumulator waits, ns */
     SPB_DEBUG_TC_HINT = 6,    /* tensor path: suspend hint of the ring waits, ns */
     SPB_DEBUG_TC_SPLIT_STAGES = 7, /* tensor path: 1 = one ring unit per stage (no half-stage units) */
+    SPB_DEBUG_TC_LAUNCH_FLAGS = 8, /* tensor path, launch-overhead measurement: 1 = launch without the
+                                      cooperative attribute, 2 = without programmatic dependent launch */
+    SPB_DEBUG_TC_DENSE_PERMILLE = 9, /* tensor path: union share of f (per mille) from which whole row
+                                        ranges stream (0: the default; above 1000: never) */
 };
 
 /* Sets one process-wide hook; applies to launches made after the call. */

@@ -132,13 +132,13 @@ static int ffn_impl(const void *w_gate, const void *w_up, const void *w_down, in
         return fail(SPB_ERR_WORKSPACE, "spb_ffn_forward: workspace too small");
     cudaStream_t st = static_cast<cudaStream_t>(stream);
 
-    // quantised weights are served by the CUDA-core path (in-register dequantisation)
-    if (path == SPB_PATH_AUTO) path = (B <= kGemvMaxBatch || wtype != SPB_W_F16) ? SPB_PATH_GEMV : SPB_PATH_TENSOR;
+    // Batches of up to four tokens stream on the CUDA cores; larger ones take
+    // the tensor-core path (fp16 or quantised rows, d a multiple of 256).
+    if (path == SPB_PATH_AUTO) path = (B <= kGemvMaxBatch || d % 256 != 0) ? SPB_PATH_GEMV : SPB_PATH_TENSOR;
     int32_t *merge = merge_idx_out ? merge_idx_out : ws.merge_idx;
     int32_t *count = count_out ? count_out : ws.counts;
 
     if (path == SPB_PATH_TENSOR) {
-        if (wtype != SPB_W_F16) return fail(SPB_ERR_UNSUPPORTED, "spb_ffn_forward: tensor path serves fp16 weights");
         if (B > 256) return fail(SPB_ERR_UNSUPPORTED, "spb_ffn_forward: tensor path serves B <= 256");
         if (d % 256 != 0) return fail(SPB_ERR_INVALID, "spb_ffn_forward: tensor path needs d % 256 == 0");
         // one cooperative launch: union, fp16 activations and the zeroed
@@ -147,6 +147,8 @@ static int ffn_impl(const void *w_gate, const void *w_up, const void *w_down, in
         L.wg = w_gate;
         L.wu = w_up;
         L.wd = w_down;
+        L.wtype = wtype;
+        L.allow_dense = merge_idx_out == nullptr;
         L.labels = idx;
         L.tok_in = tok_in;
         L.bias_g = bg;
@@ -367,6 +369,8 @@ int spb_debug_config(int key, long long value) {
         case SPB_DEBUG_TC_HINT_ACC: g_debug.hint_acc = (uint32_t)value; return SPB_OK;
         case SPB_DEBUG_TC_HINT: g_debug.hint = (uint32_t)value; return SPB_OK;
         case SPB_DEBUG_TC_SPLIT_STAGES: g_debug.split_stages = (int)value; return SPB_OK;
+        case SPB_DEBUG_TC_LAUNCH_FLAGS: g_debug.launch_flags = (int)value; return SPB_OK;
+        case SPB_DEBUG_TC_DENSE_PERMILLE: g_debug.dense_permille = (int)value; return SPB_OK;
         default: return fail(SPB_ERR_INVALID, "spb_debug_config: unknown key");
     }
 }
@@ -374,7 +378,7 @@ int spb_debug_config(int key, long long value) {
 
 int spb_ffn_launches(int B, int d, int wtype, int path) {
     if (B <= 0 || d <= 0) return 0;
-    if (path == SPB_PATH_AUTO) path = (B <= kGemvMaxBatch || wtype != SPB_W_F16) ? SPB_PATH_GEMV : SPB_PATH_TENSOR;
+    if (path == SPB_PATH_AUTO) path = (B <= kGemvMaxBatch || d % 256 != 0) ? SPB_PATH_GEMV : SPB_PATH_TENSOR;
     if (path == SPB_PATH_TENSOR) return 1;  // one cooperative tensor-core launch
     if (stream_ffn_supported(wtype, B, d)) return 1;
     int chunk = 4;  // the token-group split spb_ffn_forward makes

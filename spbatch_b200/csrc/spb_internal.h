@@ -84,6 +84,8 @@ int launch_dropin_down(const __half *wd, const float *h, float *out, const int32
 // tc_ffn.cu -- tcgen05 tensor-core path (one launch after the union)
 struct TcLaunch {
     const void *wg, *wu, *wd;
+    int wtype;                // SPB_W_F16 / SPB_W_Q8_0 / SPB_W_Q4_0 (row layout of wg, wu, wd)
+    bool allow_dense;         // whole row ranges may stream (no compacted ids requested)
     const float *labels;      // [B][f] fp32 labels, or null when tok_in is given
     const uint32_t *tok_in;   // [B][W] per-token activity bits, or null
     const float *x;           // [B][d]
@@ -111,6 +113,10 @@ struct DebugHooks {
     uint32_t hint_acc = 0;    // tensor path: suspend hint of the epilogue's accumulator waits (ns)
     uint32_t hint = 0;        // tensor path: suspend hint of the ring waits (ns)
     int split_stages = 0;     // tensor path: split gate/up stages over two ring units
+    int launch_flags = 0;     // tensor path, measurement only: 1 = no cooperative attribute, 2 = no
+                              // programmatic dependent launch
+    int dense_permille = 0;   // tensor path: union share of f (per mille) from which whole row ranges
+                              // stream (0 default, above 1000 never)
 };
 const DebugHooks &debug_hooks();
 

@@ -14,9 +14,10 @@
 //             W_gate rows with the batch, CTA rank 1 the W_up rows
 //             (tcgen05.mma.kind::f16, M = 128 rows, N = Np tokens, K = d,
 //             fp32 accumulator in TMEM).  Each ring stage holds nkb 64-wide K
-//             blocks of the rows (cp.async, a 128 * nkb-byte run per row)
-//             and the activation tile (TMA), both in the 128-byte-swizzled
-//             K-major layout the MMA reads.  The pair then trades halves: a
+//             blocks of the rows (cp.async, a 128 * nkb-byte run per row;
+//             quantised rows are expanded to fp16 by the producers) and the
+//             activation tile (TMA), both in the 128-byte-swizzled K-major
+//             layout the MMA reads.  The pair then trades halves: a
 //             CTA writes its results for the partner's 64 rows to its
 //             workspace slot and signals the partner's mbarrier (release at
 //             cluster scope); with the partner's half it forms h = act(gate,
@@ -67,6 +68,8 @@ constexpr int kTcThreads = (kTmaWarp + 1) * 32;
 constexpr int kTcWarps = kTcThreads / 32;
 constexpr int kTileM = 128;          // neurons per gate/up tile (MMA M)
 constexpr int kDnRows = 64;          // union positions per down stage
+constexpr int kBoxRows = 32;         // rows per weight TMA box when whole row ranges stream
+constexpr int kDenseMinPermille = 960;  // union share of f from which whole row ranges stream
 constexpr int kSlice = 256;          // output columns per down unit (two M = 128 MMAs)
 constexpr uint32_t kATile = 16384;   // 128 rows x 128 bytes (one 64-wide K block)
 constexpr uint32_t kDnLbo = (kDnRows / 8) * 1024;  // byte distance between 64-column blocks of a down stage
@@ -103,7 +106,14 @@ struct TcCtl {
 };
 
 struct TcArgs {
-    const __half *wg, *wu, *wd;  // [f][d]
+    const __half *wg, *wu, *wd;  // [f][d] rows (fp16), or quantised rows of rowb bytes (wtype)
+    int wtype;                   // SPB_W_F16 / SPB_W_Q8_0 / SPB_W_Q4_0
+    int64_t rowb;                // bytes per stored weight row
+    int nstg;                    // quantised weights: staging slots (stages staged ahead of the ring)
+    uint32_t stg_bytes;          // bytes of one staging slot (all producers' tasks of one stage)
+    int stg_tasks;               // task capacity of a slot (quant bytes first, then 4-byte scale pairs)
+    int dense_min;               // fp16: a union of at least this many neurons streams whole row ranges
+                                 // (every neuron a position, 2-D TMA boxes) instead of gathering rows
     const float *labels;         // [B][f] fp32 labels (> 0 active), or null with tok_in
     const uint32_t *tok_in;      // [B][W] per-token activity bits given by the caller, or null
     const float *x;              // [B][d] fp32 activations
@@ -132,13 +142,16 @@ struct TcArgs {
     uint32_t unit_bytes;
     uint64_t timeout_ns;
     uint32_t hint_acc, hint;     // suspend-time hints of the accumulator / ring waits (ns)
-    int inject;                  // test hook: 1 = CTA rank 1 never signals its results;
+    int inject;                  // test hook: 1 = CTA rank 1 never signals its results; profiling only
+                                 // (quantised producers): 8 = no expansion, 16 = no copies;
                                  // profiling only: 2 = no output reductions, 4 = no W_down copies
 };
 
 // TMA descriptors of the activations and of h (box 64 x Np, 128-byte swizzle).
 struct TcMaps {
     CUtensorMap x, h;
+    CUtensorMap wg, wu;  // [f][d] rows, box 64 x kBoxRows (dense streaming)
+    CUtensorMap wd;      // [f][d] rows, box 64 x kDnRows (dense streaming)
 };
 
 // Phase stamps written when tracing is enabled (spb_trace_enable).
@@ -257,6 +270,27 @@ __device__ __forceinline__ void tile_rows(int n, int nt, int i, int &r0, int &r1
 
 __device__ __forceinline__ int tiles_of(int n) { return (n + kTileM - 1) / kTileM; }
 
+// First position of cluster c's gate/up share.  Gathered rows: the union
+// positions split evenly.  Whole row ranges (dense): positions are neuron
+// ids, split in whole kBoxRows-row boxes (nb = f / kBoxRows rounded up).
+__device__ __forceinline__ int span_start(bool dense, int Uv, int c, int C) {
+    if (!dense) return cluster_start(Uv, c, C);
+    const int nb = (Uv + kBoxRows - 1) / kBoxRows;
+    return min(Uv, kBoxRows * (int)((uint32_t)(nb * c) / (uint32_t)C));
+}
+
+// Tile i of nt over a share of n positions: near-equal splits, in whole boxes
+// when the rows stream as boxes.
+__device__ __forceinline__ void tile_span(bool dense, int n, int nt, int i, int &r0, int &r1) {
+    if (!dense) {
+        tile_rows(n, nt, i, r0, r1);
+        return;
+    }
+    const int nb = (n + kBoxRows - 1) / kBoxRows;
+    r0 = min(n, kBoxRows * (int)((uint32_t)(nb * i) / (uint32_t)nt));
+    r1 = min(n, kBoxRows * (int)((uint32_t)(nb * (i + 1)) / (uint32_t)nt));
+}
+
 // Union chunk k of KC for the down phase: 64-aligned start, so the h tiles'
 // TMA coordinates are 16-byte aligned.
 __device__ __forceinline__ int chunk_start(int U, int k, int KC) {
@@ -294,13 +328,221 @@ __device__ __forceinline__ void emit_ids16(const uint32_t *bits, const int *pref
     }
 }
 
+// ---------------------------------------------------------------------------------
+// Quantised weights (ggml Q8_0 / Q4_0 blocks of 32 along d, in the "split" row
+// layout: the row's quant bytes, then its fp16 scales).  The MMA still reads
+// fp16 operands, so the producers expand the gathered blocks in shared memory:
+// every producer thread owns whole blocks (one 32-element block of one row =
+// a task), copies their raw bytes and their scale pair with cp.async into its
+// own part of a staging slot, and once its copies of that stage have landed
+// (cp.async.wait_group: the thread's own groups, no barrier) writes the 32
+// fp16 values into the stage's swizzled operand tile and arrives on the
+// stage's `full` barrier.  Several stages are staged ahead of the operand
+// ring, so the quant bytes in flight do not depend on the (four times larger)
+// fp16 tiles.  Values: q * scale computed in fp32 and rounded to fp16 once --
+// the product of an 8-bit integer and an fp16 scale is exact in fp32, so this
+// is the oracle's dequantised value (spbo_dequantize) rounded to the operand
+// type.
+struct QStage {
+    int t;                   // unit-step of the stage in the ring
+    int kind;                // 0 gate/up (tile rows x nkb K blocks), 1 down (positions x 256 columns)
+    int rows;                // gate/up: tile rows; down: valid positions (the rest up to 16 are zero)
+    int st;                  // gate/up: K step within the tile
+    const uint16_t *ids;     // neuron ids of the stage's rows
+};
+
+constexpr int kMaxStaging = 7;  // cp.async.wait_group takes immediates 0..7
+
+struct QuantProducer {
+    TcCtl *ctl;
+    uint8_t *ring, *stg;
+    int pt, NU, nkb;
+    const __half *wm;                // this CTA's gate/up matrix (raw rows): W_gate on rank 0, W_up on rank 1
+    int rot, KG, m;
+    int n, ntile;                    // this CTA's gate/up positions and tiles
+    const uint16_t *gu_ids, *dn_ids;
+    int Q0, Q1;                      // the down unit's positions
+
+    // The stage at unit-step t: gate/up stages first (tile t / KG, K step
+    // t % KG), then the down stages.
+    __device__ __forceinline__ QStage stage(int t) const {
+        const int ngu = ntile * KG;
+        if (t < ngu) {
+            const int i = t / KG;
+            int r0, r1;
+            tile_rows(n, ntile, i, r0, r1);
+            return QStage{t, 0, r1 - r0, t - i * KG, gu_ids + r0};
+        }
+        const int p0 = Q0 + (t - ngu) * kDnRows;
+        return QStage{t, 1, min(kDnRows, Q1 - p0), 0, dn_ids + (p0 - Q0)};
+    }
+
+    // tasks of a stage: gate/up rows x 2 nkb blocks, down positions x 8 blocks
+    __device__ __forceinline__ int tasks_of(const TcArgs &a, const QStage &q) const {
+        return q.kind == 0 ? q.rows * 2 * nkb : q.rows * 8;
+    }
+    // Task i: its MMA row r (gate/up: the tile row; down: the position),
+    // block blk within the stage, global block index gb along d.
+    __device__ __forceinline__ void task_of(const TcArgs &a, const QStage &q, int i, int &r, int &blk, int &gb) const {
+        if (q.kind == 0) {
+            const int lb = 2 * nkb;
+            r = i / lb;
+            blk = i - r * lb;
+            gb = ((q.st + rot) % KG) * lb + blk;
+        } else {
+            r = i >> 3;
+            blk = i & 7;
+            gb = m * 8 + blk;
+        }
+    }
+    __device__ __forceinline__ void task_src(const TcArgs &a, const QStage &q, int i, const uint8_t *&row, int &gb, int &r,
+                                             int &blk) const {
+        task_of(a, q, i, r, blk, gb);
+        if (q.kind == 0) {
+            row = reinterpret_cast<const uint8_t *>(wm) + (int64_t)q.ids[r] * a.rowb;
+        } else {
+            row = reinterpret_cast<const uint8_t *>(a.wd) + (int64_t)q.ids[r] * a.rowb;
+        }
+    }
+
+    __device__ __forceinline__ void issue(const TcArgs &a, const QStage &q, int slot) const {
+        const uint32_t sq = smem_u32(stg + (size_t)slot * a.stg_bytes);
+        const uint32_t ss = sq + (uint32_t)a.stg_tasks * (a.wtype == SPB_W_Q8_0 ? 32u : 16u);
+        const int nt = (a.inject & 16) ? 0 : tasks_of(a, q);
+        const int sco = a.wtype == SPB_W_Q8_0 ? a.d : a.d / 2;  // scales after the quant bytes
+        for (int i = pt; i < nt; i += kProducerThreads) {
+            const uint8_t *row;
+            int gb, r, blk;
+            task_src(a, q, i, row, gb, r, blk);
+            if (a.wtype == SPB_W_Q8_0) {
+                cp_async16_full(sq + i * 32, row + gb * 32);
+                cp_async16_full(sq + i * 32 + 16, row + gb * 32 + 16);
+            } else {
+                cp_async16_full(sq + i * 16, row + gb * 16);
+            }
+            cp_async4(ss + i * 4, row + sco + (gb & ~1) * 2);
+        }
+        cp_async_commit();
+    }
+
+    // The oldest staged stage has landed (this thread's part): expand it into
+    // its ring unit once the MMAs have released the unit.
+    __device__ __forceinline__ bool finish(const TcArgs &a, const QStage &q, int slot) const {
+        if (pt == 0) stage_stamp(a, q.t, 3);
+        if (!ring_wait_empty(q.t, NU, ctl, a)) return false;
+        if (pt == 0) stage_stamp(a, q.t, 0);
+        const uint8_t *sq = stg + (size_t)slot * a.stg_bytes;
+        const uint8_t *ss = sq + (size_t)a.stg_tasks * (a.wtype == SPB_W_Q8_0 ? 32 : 16);
+        const uint32_t ubase = smem_u32(ring + (size_t)(q.t % NU) * a.unit_bytes);
+        const int nt = (a.inject & 8) ? 0 : tasks_of(a, q);
+        for (int i = pt; i < nt; i += kProducerThreads) {
+            int r, blk, gb;
+            task_of(a, q, i, r, blk, gb);
+            // the block's scale in both halves of a half2
+            const uint32_t sp = *reinterpret_cast<const uint32_t *>(ss + i * 4);
+            const uint32_t sc2 = __byte_perm(sp, 0, (gb & 1) ? 0x3232 : 0x1010);
+            uint32_t raw[8];
+            if (a.wtype == SPB_W_Q8_0) {
+                const uint4 v0 = *reinterpret_cast<const uint4 *>(sq + i * 32);
+                const uint4 v1 = *reinterpret_cast<const uint4 *>(sq + i * 32 + 16);
+                raw[0] = v0.x; raw[1] = v0.y; raw[2] = v0.z; raw[3] = v0.w;
+                raw[4] = v1.x; raw[5] = v1.y; raw[6] = v1.z; raw[7] = v1.w;
+            } else {
+                const uint4 v = *reinterpret_cast<const uint4 *>(sq + i * 16);
+                raw[0] = v.x; raw[1] = v.y; raw[2] = v.z; raw[3] = v.w;
+            }
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                // Elements 8c .. 8c + 7 of the block as four half2 pairs.  An
+                // integer u < 1024 placed in the mantissa of 1024.0 (0x6400)
+                // is the fp16 value 1024 + u exactly; subtracting the offset
+                // gives q (Q8_0: u = q + 128) or q - 8 (Q4_0: u = nibble)
+                // exactly, and one fp16 multiply by the scale rounds the exact
+                // product once -- the fp32 product rounded to fp16.
+                uint32_t wd[2];
+                uint32_t off;
+                if (a.wtype == SPB_W_Q8_0) {
+                    wd[0] = raw[2 * c] ^ 0x80808080u;
+                    wd[1] = raw[2 * c + 1] ^ 0x80808080u;
+                    off = 0x64806480u;  // 1152.0 in both halves
+                } else {
+                    // element j (< 16) is the low nibble of byte j, element j + 16 its high nibble
+                    const int sh = c < 2 ? 0 : 4;
+                    wd[0] = (raw[(c & 1) * 2] >> sh) & 0x0f0f0f0fu;
+                    wd[1] = (raw[(c & 1) * 2 + 1] >> sh) & 0x0f0f0f0fu;
+                    off = 0x64086408u;  // 1032.0 in both halves
+                }
+                uint32_t h[4];
+#pragma unroll
+                for (int p = 0; p < 4; ++p) {
+                    const uint32_t u = __byte_perm(wd[p >> 1], 0x64646464u, (p & 1) ? 0x4342 : 0x4140);
+                    __half2 v = __hsub2(*reinterpret_cast<const __half2 *>(&u),
+                                        *reinterpret_cast<const __half2 *>(&off));
+                    v = __hmul2(v, *reinterpret_cast<const __half2 *>(&sc2));
+                    h[p] = *reinterpret_cast<uint32_t *>(&v);
+                }
+                const uint4 o = make_uint4(h[0], h[1], h[2], h[3]);
+                uint32_t dst;
+                if (q.kind == 0) {
+                    const int cc = (blk & 1) * 4 + c;
+                    dst = ubase + (blk >> 1) * kATile + r * 128 + ((cc ^ (r & 7)) << 4);
+                } else {
+                    const int c8 = (blk & 1) * 4 + c, kr = r & 7;
+                    dst = ubase + (blk >> 1) * kDnLbo + (r >> 3) * 1024 + kr * 128 + ((c8 ^ kr) << 4);
+                }
+                st_shared_v4(dst, o);
+            }
+        }
+        if (q.kind == 1) {
+            // positions past the chunk, up to the next multiple of 16: zero rows
+            const int nr16 = (q.rows + 15) & ~15;
+            for (int i = q.rows * 32 + pt; i < nr16 * 32; i += kProducerThreads) {
+                const int r = i >> 5, c = i & 31, mb = c >> 3, c8 = c & 7, kr = r & 7;
+                st_shared_v4(ubase + mb * kDnLbo + (r >> 3) * 1024 + kr * 128 + ((c8 ^ kr) << 4),
+                             make_uint4(0u, 0u, 0u, 0u));
+            }
+        }
+        // (the MMA issuer fences its view of these generic-proxy writes
+        // against the async proxy once the stage's barrier completes)
+        mbar_arrive(&ctl->full[q.t % NU]);
+        if (pt == 0) stage_stamp(a, q.t, 1);
+        return true;
+    }
+
+    // Stage t's copies are issued into staging slot t % nstg; stage
+    // t - nstg, whose slot that was, is expanded first (its copies are this
+    // thread's oldest outstanding group).
+    __device__ __forceinline__ bool step(const TcArgs &a, int t) const {
+        if (t >= a.nstg) {
+            cp_async_wait(a.nstg - 1);
+            if (!finish(a, stage(t - a.nstg), (t - a.nstg) % a.nstg)) return false;
+        }
+        issue(a, stage(t), t % a.nstg);
+        return true;
+    }
+
+    // Expands the stages still staged after stage `end` - 1 was issued.
+    __device__ __forceinline__ bool drain(const TcArgs &a, int end) const {
+        for (int t = max(0, end - a.nstg); t < end; ++t) {
+            cp_async_wait(min(end - 1 - t, kMaxStaging));
+            if (!finish(a, stage(t), t % a.nstg)) return false;
+        }
+        return true;
+    }
+};
+
+// kQuant: the producers expand quantised rows (a separate instantiation, so
+// the fp16 kernel carries none of that code).
+template <bool kQuant>
 __global__ void __launch_bounds__(kTcThreads, 1)
 ffn_tc_kernel(const __grid_constant__ TcMaps maps, const TcArgs a) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int NU = a.nu, GW = a.gw, W = a.W, Np = a.Np, nkb = a.nkb, nbuf = a.nbuf;
     uint8_t *ring = smem;
-    TcCtl *ctl = reinterpret_cast<TcCtl *>(ring + (size_t)NU * a.unit_bytes);
+    // quantised weights: staging slots for the raw blocks, after the ring
+    uint8_t *stg = ring + (size_t)NU * a.unit_bytes;
+    TcCtl *ctl = reinterpret_cast<TcCtl *>(stg + (size_t)a.nstg * a.stg_bytes);
     uint32_t *tokmask = reinterpret_cast<uint32_t *>(ctl + 1);  // [8][128] per tile row: its tokens' bits
     uint16_t *gu_ids = reinterpret_cast<uint16_t *>(tokmask + 8 * kTileM);  // [max_gu]
     uint16_t *dn_ids = gu_ids + a.max_gu;                                    // [max_dn]
@@ -443,20 +685,25 @@ ffn_tc_kernel(const __grid_constant__ TcMaps maps, const TcArgs a) {
     scan_popc(bits, W, prefix, wtot);  // ends with __syncthreads
     if (tid == 0) stamp(a, kTrScan);
     const int U = prefix[W];
+    // A union covering most of the neurons streams whole row ranges: every
+    // neuron is a position (Uv = f), rows arrive as 2-D TMA boxes at the
+    // copy engine's rate, and the inactive neurons' h is zero by the mask.
+    const bool dense = !kQuant && U >= a.dense_min;
+    const int Uv = dense ? a.f : U;
     // gate/up work of this cluster
-    const int P0 = cluster_start(U, clu, nclu);
-    const int n = cluster_start(U, clu + 1, nclu) - P0;
+    const int P0 = span_start(dense, Uv, clu, nclu);
+    const int n = span_start(dense, Uv, clu + 1, nclu) - P0;
     const int ntile = tiles_of(n);
     // down unit of this CTA: 256-column slice m of union chunk k
     const int MT = a.d / kSlice;
     const int unit = blockIdx.x;
     const bool has_dn = unit < MT * a.KC;
     const int m = unit % MT, k = unit / MT;
-    const int Q0 = has_dn ? chunk_start(U, k, a.KC) : 0;
-    const int Q1 = has_dn ? chunk_start(U, k + 1, a.KC) : 0;
+    const int Q0 = has_dn ? chunk_start(Uv, k, a.KC) : 0;
+    const int Q1 = has_dn ? chunk_start(Uv, k + 1, a.KC) : 0;
     const int ndn = (Q1 - Q0 + kDnRows - 1) / kDnRows;  // down stages
     if (blockIdx.x == 0 && tid == 0) *a.count_out = U;
-    emit_ids16(bits, prefix, W, P0, P0 + n, gu_ids, warp, kTcWarps);
+    if (!dense) emit_ids16(bits, prefix, W, P0, P0 + n, gu_ids, warp, kTcWarps);
     if (tid == 0) stamp(a, kTrEmitGu);
     __syncthreads();
     tc_fence_after();
@@ -468,8 +715,25 @@ ffn_tc_kernel(const __grid_constant__ TcMaps maps, const TcArgs a) {
 
     const int KG = a.d / (64 * nkb);
 
-    if (warp >= kProducerWarp0 && warp < kMmaWarp) {
+    if (kQuant && warp >= kProducerWarp0 && warp < kMmaWarp) {
+        // ------------------------------------------------- producers (quantised)
+        const int pt = tid - kProducerWarp0 * 32;
+        const QuantProducer qp{ctl, ring, stg, pt, NU, nkb, rank ? a.wu : a.wg, (KG ? clu % KG : 0), KG, m, n, ntile,
+                               gu_ids, dn_ids, Q0, Q1};
+        bool ok = !ctl->abort;
+        const int ngu = ntile * KG, total = ngu + ndn;
+        int t = 0;
+        for (; t < total && ok; ++t) {
+            // the down stages' ids come from the epilogue warps
+            if (t == ngu) ok = wait_bar(&ctl->ids_ready, 0, ctl, a, kErrTimeoutAcc, a.hint);
+            if (ok) ok = qp.step(a, t);
+        }
+        if (ok) qp.drain(a, total);
+        // Every copy this thread issued lands before the CTA can exit.
+        cp_async_wait_all();
+    } else if (warp >= kProducerWarp0 && warp < kMmaWarp && !dense) {
         // ------------------------------------------------------------ producers
+        // (idle when whole row ranges stream: the TMA warp moves the rows)
         const int pt = tid - kProducerWarp0 * 32, pw = pt >> 5;
         const bool leader = pt == 0;  // stamps only
         const __half *wm = rank ? a.wu : a.wg;
@@ -542,31 +806,40 @@ ffn_tc_kernel(const __grid_constant__ TcMaps maps, const TcArgs a) {
             if (bits_in && ok) ok = wait_count(a.gbar + 1, gridDim.x, ctl, a);
             asm volatile("fence.proxy.async.global;" ::: "memory");
             const int rot = KG ? clu % KG : 0;
+            const CUtensorMap *wmap = rank ? &maps.wu : &maps.wg;
             for (int i = 0; i < ntile && ok; ++i) {
+                int r0 = 0, r1 = 0;
+                if (dense) tile_span(true, n, ntile, i, r0, r1);
+                // whole row ranges: the tile's rows as kBoxRows-row boxes per K block
+                const int nbx = dense ? (r1 - r0 + kBoxRows - 1) / kBoxRows : 0;
                 for (int st = 0; st < KG; ++st, t += GW) {
                     if (!(ok = ring_wait_empty(t, NU, ctl, a))) break;
                     const uint32_t sbase = smem_u32(ring + (size_t)(t % NU) * a.unit_bytes);
                     const int kbase = ((st + rot) % KG) * 64 * nkb;
                     uint64_t *bar = &ctl->tma[t % NU];
-                    mbar_arrive_expect_tx(bar, (uint32_t)nkb * Np * 128);
+                    mbar_arrive_expect_tx(bar, (uint32_t)nkb * (Np + nbx * kBoxRows) * 128);
                     if (GW == 2) mbar_arrive(&ctl->tma[(t + 1) % NU]);
-                    for (int kb = 0; kb < nkb; ++kb)
+                    for (int kb = 0; kb < nkb; ++kb) {
                         tma_load_2d(sbase + nkb * kATile + kb * Np * 128, &maps.x, bar, kbase + kb * 64, 0);
+                        for (int bx = 0; bx < nbx; ++bx)
+                            tma_load_2d(sbase + kb * kATile + bx * kBoxRows * 128, wmap, bar, kbase + kb * 64,
+                                        P0 + r0 + bx * kBoxRows);
+                    }
                 }
             }
             // clusters [.., cl_ok) are known to have published all their h
             int cl_ok = 0;
-            while (cl_ok + 1 < nclu && cluster_start(U, cl_ok + 1, nclu) <= Q0) ++cl_ok;
+            while (cl_ok + 1 < nclu && span_start(dense, Uv, cl_ok + 1, nclu) <= Q0) ++cl_ok;
             for (int st = 0; st < ndn && ok; ++st, ++t) {
                 if (!(ok = ring_wait_empty(t, NU, ctl, a))) break;
                 const int p0 = Q0 + st * kDnRows;
                 const int nr16 = (min(kDnRows, Q1 - p0) + 15) & ~15;
                 // h of positions [p0, p0 + nr16): wait for every cluster that
                 // owns one of them and has not been confirmed yet
-                const int last = min(p0 + nr16, U) - 1;
+                const int last = min(p0 + nr16, Uv) - 1;
                 bool fresh = false;
-                while (ok && cl_ok < nclu && cluster_start(U, cl_ok, nclu) <= last) {
-                    const int cn = cluster_start(U, cl_ok + 1, nclu) - cluster_start(U, cl_ok, nclu);
+                while (ok && cl_ok < nclu && span_start(dense, Uv, cl_ok, nclu) <= last) {
+                    const int cn = span_start(dense, Uv, cl_ok + 1, nclu) - span_start(dense, Uv, cl_ok, nclu);
                     ok = wait_count(a.ready + cl_ok, 2u * (uint32_t)tiles_of(cn), ctl, a);
                     fresh = true;
                     ++cl_ok;
@@ -577,8 +850,13 @@ ffn_tc_kernel(const __grid_constant__ TcMaps maps, const TcArgs a) {
                 // the async proxy
                 if (fresh) asm volatile("fence.proxy.async.global;" ::: "memory");
                 const uint32_t sbase = smem_u32(ring + (size_t)(t % NU) * a.unit_bytes);
-                mbar_arrive_expect_tx(&ctl->tma[t % NU], (uint32_t)Np * 128);
+                mbar_arrive_expect_tx(&ctl->tma[t % NU], (uint32_t)Np * 128 + (dense ? kDnWBytes : 0u));
                 tma_load_2d(sbase + kDnWBytes, &maps.h, &ctl->tma[t % NU], p0, 0);
+                // whole row ranges: the 64 W_down rows as four 64-column boxes
+                // (rows past f read as zero)
+                if (dense)
+                    for (int mb = 0; mb < 4; ++mb)
+                        tma_load_2d(sbase + mb * kDnLbo, &maps.wd, &ctl->tma[t % NU], m * kSlice + mb * 64, p0);
             }
             // Every TMA this thread issued lands before the CTA can exit: the
             // last NU unit-steps it armed each complete their phase.
@@ -607,9 +885,10 @@ ffn_tc_kernel(const __grid_constant__ TcMaps maps, const TcArgs a) {
                 return true;
             };
             int t = 0;  // unit-step
+            // (whole row ranges: the TMA barrier alone covers the stage)
             auto wait_unit = [&](int q) -> bool {
                 const uint32_t par = (uint32_t)(q / NU) & 1u;
-                return wait_bar(&ctl->full[q % NU], par, ctl, a, kErrTimeoutFull, a.hint) &&
+                return (dense || wait_bar(&ctl->full[q % NU], par, ctl, a, kErrTimeoutFull, a.hint)) &&
                        wait_bar(&ctl->tma[q % NU], par, ctl, a, kErrTimeoutFull, a.hint);
             };
             // A two-unit stage is complete when its first unit is: the
@@ -704,24 +983,26 @@ ffn_tc_kernel(const __grid_constant__ TcMaps maps, const TcArgs a) {
         const bool signal = !(a.inject == 1 && rank == 1);
         const bool mine_half = (e >> 6) == (int)rank;  // rows this CTA finishes (warp-uniform)
         // the down unit's ids, while the gate/up stages stream
-        emit_ids16(bits, prefix, W, Q0, Q1, dn_ids, warp, kEpiWarps);
+        if (!dense) emit_ids16(bits, prefix, W, Q0, Q1, dn_ids, warp, kEpiWarps);
         if (e == 0) stamp(a, kTrEmitDn);
         mbar_arrive(&ctl->ids_ready);
         int ub = 0;
         bool ok = named_bar_and(kEpiBar, 128, !ctl->abort);
         for (int i = 0; i < ntile && ok; ++i) {
             int r0, r1;
-            tile_rows(n, ntile, i, r0, r1);
+            tile_span(dense, n, ntile, i, r0, r1);
             const int rows = r1 - r0;
             const bool valid = e < rows;
-            const int j = valid ? gu_ids[r0 + e] : 0;
+            const int j = valid ? (dense ? P0 + r0 + e : gu_ids[r0 + e]) : 0;
             // While the gate/up MMAs run: this row's per-token activity bits
             // (bit t of word t/32), so forming h reads no global memory.
             if (mine_half) {
                 for (int t0 = 0; t0 < Np; t0 += 32) {
                     uint32_t word = 0;
                     if (!a.per_token) {
-                        word = ~0u;
+                        // union semantics: every union neuron for every token
+                        // (whole row ranges also hold neurons outside it)
+                        word = (!dense || (valid && ((bits[j >> 5] >> (j & 31)) & 1u))) ? ~0u : 0u;
                     } else if (valid && a.tok_in) {
                         const uint32_t *mcol = a.tok_in + (j >> 5);
 #pragma unroll 8
@@ -798,17 +1079,17 @@ ffn_tc_kernel(const __grid_constant__ TcMaps maps, const TcArgs a) {
                         }
                     }
                 }
-                if (valid) a.merge_out[pos] = j;
+                if (valid && !dense) a.merge_out[pos] = j;
             }
             mbar_arrive_remote(peer_free);  // the partner's slot has been read
             tc_fence_before();
             mbar_arrive(&ctl->acc_empty[buf]);
-            // positions [U, U rounded up to 64) of h are read by the last
+            // positions [Uv, Uv rounded up to 64) of h are read by the last
             // down stage: the cluster holding position U - 1 zeroes them
-            if (i == ntile - 1 && P0 + n == U && rank == 0) {
-                const int tail = ((U + 63) & ~63) - U;
+            if (i == ntile - 1 && P0 + n == Uv && rank == 0) {
+                const int tail = ((Uv + 63) & ~63) - Uv;
                 for (int q = e; q < tail * Np; q += 128)
-                    a.h16[(int64_t)(q / tail) * a.fpad + U + q % tail] = __float2half_rn(0.0f);
+                    a.h16[(int64_t)(q / tail) * a.fpad + Uv + q % tail] = __float2half_rn(0.0f);
             }
             // publish: h rows of this tile (and the zero tail) visible GPU-wide
             // before the cluster's counter moves
@@ -992,16 +1273,61 @@ static Geometry pick_geometry(int Np, int W, int max_gu, int max_dn, int d, int 
     return best;
 }
 
+// Quantised weights: ring units hold the expanded fp16 stages (whole-stage
+// units) and the staging slots hold the raw blocks of nstg stages.
+struct QGeometry {
+    Geometry g;
+    int nstg, tasks;
+    uint32_t slot;
+};
+
+static QGeometry pick_geometry_quant(int Np, int W, int max_gu, int max_dn, int d, int wtype, int force_nkb) {
+    const size_t fixed = fixed_smem(Np, W, max_gu, max_dn);
+    const size_t budget = 227 * 1024;
+    const uint32_t qb = wtype == SPB_W_Q8_0 ? 32u : 16u;
+    const uint32_t dn = (kDnWBytes + (uint32_t)Np * 128 + 1023) & ~1023u;
+    QGeometry best{};
+    size_t best_score = 0;
+    for (int nkb = 4; nkb >= 1; nkb >>= 1) {
+        if (force_nkb && nkb != force_nkb) continue;
+        if ((d / 64) % nkb) continue;
+        const uint32_t gu = ((uint32_t)nkb * (kATile + (uint32_t)Np * 128) + 1023) & ~1023u;
+        const uint32_t unit = gu > dn ? gu : dn;
+        const int tasks = std::max(kTileM * 2 * nkb, kDnRows * 8);
+        const uint32_t slot = ((uint32_t)tasks * (qb + 4) + 127) & ~127u;
+        for (int nu = 2; nu <= kMaxUnits; ++nu) {
+            if (fixed + (size_t)nu * unit + 2u * slot > budget) break;
+            const int nstg = (int)std::min<size_t>((budget - fixed - (size_t)nu * unit) / slot, kMaxStaging);
+            // Every stage costs a round trip through the ring (the activation
+            // tile's TMA, the expansion, the MMA's release), so the widest
+            // stages win; then the stages staged ahead, then a third unit.
+            const size_t score = (size_t)nkb * 1000000 + (size_t)nstg * 10 + (nu >= 3 ? 1 : 0);
+            if (score > best_score) {
+                best_score = score;
+                best = QGeometry{Geometry{nkb, nu, 1, unit, fixed + (size_t)nu * unit + (size_t)nstg * slot}, nstg,
+                                 tasks, slot};
+            }
+        }
+    }
+    return best;
+}
+
 // Clusters of two that can be resident at once with `smem` bytes per CTA
 // (cached per device and size).
-static int max_clusters(size_t smem, int sms) {
+static int max_clusters(const void *kernel, size_t smem, int sms) {
+    struct Entry {
+        int dev;
+        const void *kernel;
+        size_t smem;
+        int n;
+    };
     static std::mutex mu;
-    static std::vector<std::pair<std::pair<int, size_t>, int>> cache;
+    static std::vector<Entry> cache;
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return sms / 2;
     std::lock_guard<std::mutex> lk(mu);
     for (auto &e : cache)
-        if (e.first.first == dev && e.first.second == smem) return e.second;
+        if (e.dev == dev && e.kernel == kernel && e.smem == smem) return e.n;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * (sms / 2));
     cfg.blockDim = dim3(kTcThreads);
@@ -1014,12 +1340,12 @@ static int max_clusters(size_t smem, int sms) {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, (const void *)ffn_tc_kernel, &cfg) != cudaSuccess || n <= 0) {
+    if (cudaOccupancyMaxActiveClusters(&n, kernel, &cfg) != cudaSuccess || n <= 0) {
         cudaGetLastError();
         n = sms / 2;
     }
     n = std::min(n, sms / 2);
-    cache.push_back({{dev, smem}, n});
+    cache.push_back(Entry{dev, kernel, smem, n});
     return n;
 }
 
@@ -1032,6 +1358,9 @@ int launch_ffn_tc(const TcLaunch &L, cudaStream_t st) {
     a.wg = static_cast<const __half *>(L.wg);
     a.wu = static_cast<const __half *>(L.wu);
     a.wd = static_cast<const __half *>(L.wd);
+    a.wtype = L.wtype;
+    a.rowb = L.wtype == SPB_W_F16 ? (int64_t)L.d * 2
+                                  : (L.wtype == SPB_W_Q8_0 ? (int64_t)L.d + L.d / 16 : (int64_t)L.d / 2 + L.d / 16);
     a.labels = L.labels;
     a.tok_in = L.tok_in;
     a.x = L.x;
@@ -1064,6 +1393,7 @@ int launch_ffn_tc(const TcLaunch &L, cudaStream_t st) {
     a.xdsm = Np <= kXdsmMaxNp ? 1 : 0;
 
     const int sms = std::min(L.grid, kMaxTcGrid);
+    const void *kernel = L.wtype == SPB_W_F16 ? (const void *)ffn_tc_kernel<false> : (const void *)ffn_tc_kernel<true>;
     const int MT = L.d / kSlice;
     // size the id tables for the most clusters this device can hold, then
     // check the launch against the real count
@@ -1074,10 +1404,22 @@ int launch_ffn_tc(const TcLaunch &L, cudaStream_t st) {
         a.KC = std::max(1, (2 * nclu) / MT);
         a.max_gu = (L.f + nclu - 1) / nclu + 1;
         a.max_dn = (L.f + a.KC - 1) / a.KC + 128;
-        g = pick_geometry(Np, a.W, a.max_gu, a.max_dn, L.d, dbg.nkb, dbg.stages, dbg.split_stages != 0);  // test hook: 1 = whole-stage units
+        if (L.wtype == SPB_W_F16) {
+            g = pick_geometry(Np, a.W, a.max_gu, a.max_dn, L.d, dbg.nkb, dbg.stages, dbg.split_stages != 0);
+            a.nstg = 0;
+            a.stg_bytes = 0;
+            a.stg_tasks = 0;
+        } else {
+            const QGeometry q = pick_geometry_quant(Np, a.W, a.max_gu, a.max_dn, L.d, L.wtype, dbg.nkb);
+            g = q.g;
+            a.nstg = q.nstg;
+            a.stg_bytes = q.slot;
+            a.stg_tasks = q.tasks;
+            if (g.nu >= 2 && q.nstg < 2) g.nu = 0;
+        }
         if (g.nu < 2) return fail(SPB_ERR_UNSUPPORTED, "tensor path: shared memory too small for two stages");
-        if ((rc = ensure_smem((const void *)ffn_tc_kernel, g.smem))) return rc;
-        const int fit = max_clusters(g.smem, sms);
+        if ((rc = ensure_smem(kernel, g.smem))) return rc;
+        const int fit = max_clusters(kernel, g.smem, sms);
         if (fit >= nclu) break;
         nclu = std::max(1, fit);
     }
@@ -1089,6 +1431,22 @@ int launch_ffn_tc(const TcLaunch &L, cudaStream_t st) {
     TcMaps maps;
     if ((rc = tensor_map(L.x16, L.d, Np, Np, &maps.x))) return rc;
     if ((rc = tensor_map(L.h16, L.fpad, Np, Np, &maps.h))) return rc;
+    // Whole row ranges stream when the union covers nearly all neurons (fp16
+    // rows; not when the compacted ids are asked for).  Measured on B200 (7B):
+    // at U/f = 0.85 (B = 32) streaming whole ranges took 87 us against 69 us
+    // gathering -- the kBoxRows-aligned shares leave clusters with a 96- and
+    // a 64-row tile, twice the ring stages -- while at U/f = 0.99 (B = 64) it
+    // took 95.9 us against 99.9 us.
+    a.dense_min = INT32_MAX;
+    if (L.wtype == SPB_W_F16 && L.allow_dense) {
+        const int permille = dbg.dense_permille ? dbg.dense_permille : kDenseMinPermille;
+        if (permille <= 1000) {
+            a.dense_min = (int)(((int64_t)L.f * permille + 999) / 1000);
+            if ((rc = tensor_map(L.wg, L.d, L.f, kBoxRows, &maps.wg))) return rc;
+            if ((rc = tensor_map(L.wu, L.d, L.f, kBoxRows, &maps.wu))) return rc;
+            if ((rc = tensor_map(L.wd, L.d, L.f, kDnRows, &maps.wd))) return rc;
+        }
+    }
 
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * nclu);
@@ -1107,9 +1465,20 @@ int launch_ffn_tc(const TcLaunch &L, cudaStream_t st) {
     attr[1].val.cooperative = 1;
     attr[2].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[2].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 3;
-    SPB_CUDA_TRY(cudaLaunchKernelEx(&cfg, ffn_tc_kernel, maps, a));
+    // measurement hook (debug library only): drop attributes to see their cost
+    int na = 0;
+    cudaLaunchAttribute use[3];
+    for (int i = 0; i < 3; ++i) {
+        if (i == 1 && (dbg.launch_flags & 1)) continue;
+        if (i == 2 && (dbg.launch_flags & 2)) continue;
+        use[na++] = attr[i];
+    }
+    cfg.attrs = use;
+    cfg.numAttrs = na;
+    if (L.wtype == SPB_W_F16)
+        SPB_CUDA_TRY(cudaLaunchKernelEx(&cfg, ffn_tc_kernel<false>, maps, a));
+    else
+        SPB_CUDA_TRY(cudaLaunchKernelEx(&cfg, ffn_tc_kernel<true>, maps, a));
     return SPB_OK;
 }
 

@@ -107,7 +107,7 @@ def test_tensor_path_rejects_before_launch(spb):
     rc = L.spb_ffn_forward(fake, fake, fake, 0, fake, fake, 8, 384, 1024, 0, 1, 2, fake, None, None, fake,
                            1 << 40, None)
     assert rc == 1 and b"d % 256" in L.spb_last_error()
-    # quantised weights on the tensor path
-    rc = L.spb_ffn_forward(fake, fake, fake, 1, fake, fake, 8, 4096, 1024, 0, 1, 2, fake, None, None, fake,
+    # more than 256 tokens
+    rc = L.spb_ffn_forward(fake, fake, fake, 1, fake, fake, 257, 4096, 1024, 0, 1, 2, fake, None, None, fake,
                            1 << 40, None)
-    assert rc == 4 and b"fp16" in L.spb_last_error()
+    assert rc == 4 and b"B > 256" in L.spb_last_error()
