@@ -160,6 +160,7 @@ static int ffn_impl(const void *w_gate, const void *w_up, const void *w_down, in
         L.ready = ws.ready;
         L.fpad = ws.fpad;
         L.seg_bits = ws.seg_bits;
+        L.tc_bits = ws.tc_bits;
         L.tok_bits = ws.tok_bits;
         L.out = out;
         L.merge_out = merge;

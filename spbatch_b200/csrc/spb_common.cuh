@@ -53,6 +53,7 @@ struct Workspace {
     unsigned long long *zero_flag;   // [1] streaming kernel: launch number + 1 once `out` is zeroed
     uint32_t *tok_bits;    // [B][W] per-token activity bits
     uint32_t *seg_bits;    // [S][W] per-segment union bits
+    uint32_t *tc_bits;     // [W] tensor path: batch union accumulated by atomic OR (zero between launches)
     int32_t *merge_idx;    // [S][f] compacted ascending neuron ids
     int32_t *counts;       // [S + 1] per-segment counts (+1 spare)
     __half *h;             // [f][B] fp16 intermediate of the CUDA-core path
@@ -94,6 +95,7 @@ inline Workspace carve_workspace(void *base, int B, int d, int f, int group) {
     w.gbar = sync ? sync + 40 : nullptr;
     w.tok_bits = (uint32_t *)take(sizeof(uint32_t) * (size_t)B * W);
     w.seg_bits = (uint32_t *)take(sizeof(uint32_t) * (size_t)S * W);
+    w.tc_bits = (uint32_t *)take(sizeof(uint32_t) * (size_t)W);
     w.merge_idx = (int32_t *)take(sizeof(int32_t) * (size_t)S * f);
     w.counts = (int32_t *)take(sizeof(int32_t) * (size_t)(S + 1));
     w.h = (__half *)take(sizeof(__half) * (size_t)f * B);

@@ -92,6 +92,7 @@ struct TcLaunch {
     __half *x16;              // [Np][d] workspace
     __half *h16;              // [Np][fpad] workspace
     uint32_t *seg_bits, *tok_bits;
+    uint32_t *tc_bits;        // [W] union words by atomic OR, zero on entry (the launch re-zeroes them)
     float *out;
     int32_t *merge_out, *count_out;
     float *xchg;              // [grid][Np][64] partner-exchange slots

@@ -10,10 +10,10 @@
 // grid-wide step is needed.  B >= 2: reading all B rows in every CTA costs
 // B x f x 4 bytes of hot-line L2 traffic per SM, so each CTA scans its share
 // of the 32-neuron words, publishes the ballots to the workspace, and after a
-// grid barrier (the launch is then cooperative) reads all words back.  The CTA
-// that takes the launch's first ticket (per-CTA tickets of a monotonic
-// counter) zeroes `out` and publishes the launch number; the other CTAs check
-// it only before their final reductions.
+// grid barrier (the launch is then cooperative) reads all words back.  CTA 0
+// zeroes `out` and publishes the launch number (taken from per-CTA tickets of
+// a monotonic counter); the other CTAs check it only before their final
+// reductions.
 //
 // Rows.  Every CTA rebuilds the ascending union list from the words (one
 // block scan) and takes an equal contiguous share of it, so no CTA holds more
@@ -67,7 +67,6 @@ struct SfCtl {
     uint64_t full[kSfMaxStages];
     uint64_t empty[kSfMaxStages];
     unsigned long long launch;
-    int zeroer;  // this CTA took the launch's first ticket: it zeroes `out`
     volatile int abort;
     int U;
 };
@@ -273,21 +272,14 @@ __global__ void __launch_bounds__(kSfThreads, 1) stream_ffn_kernel(const SfArgs 
         }
     }
 
-    // ---- launch number; the first CTA to start zeroes `out` ----
+    // ---- launch number; CTA 0 zeroes `out` ----
     // Every CTA takes a ticket from a monotonic counter; launches are stream
     // ordered (a dependent launch waits above for its predecessor), so all
     // tickets of one launch precede the next launch's and ticket / grid is
-    // the launch number.  The CTA holding the launch's first ticket -- one
-    // that is running, whatever the others' residency -- zeroes `out` and
-    // then publishes launch + 1; the other CTAs check the flag only before
-    // their final reductions.
-    if (tid == 0) {
-        const unsigned long long tk = atomicAdd(a.launch_ctr, 1ull);
-        ctl->launch = tk / gridDim.x;
-        ctl->zeroer = (tk % gridDim.x) == 0;
-    }
-    __syncthreads();
-    if (ctl->zeroer) {
+    // the launch number.  CTA 0 zeroes `out` and then publishes launch + 1;
+    // the other CTAs check the flag only before their final reductions.
+    if (tid == 0) ctl->launch = atomicAdd(a.launch_ctr, 1ull) / gridDim.x;
+    if (blockIdx.x == 0) {
         const int n4 = a.B * a.d / 4;
         for (int q = tid; q < n4; q += kSfThreads)
             reinterpret_cast<float4 *>(a.out)[q] = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -394,7 +386,7 @@ __global__ void __launch_bounds__(kSfThreads, 1) stream_ffn_kernel(const SfArgs 
         }
     }
     __syncthreads();
-    if (ctl->zeroer && tid == 0) {
+    if (blockIdx.x == 0 && tid == 0) {
         __threadfence();
         st_release_u64(a.zero_flag, ctl->launch + 1);
     }
@@ -634,7 +626,7 @@ __global__ void __launch_bounds__(kSfThreads, 1) stream_ffn_kernel(const SfArgs 
         }
         if (tr && tid == 0) tr[5] = globaltimer();
 
-        // `out` must have been zeroed by the first CTA (long done in practice).
+        // `out` must have been zeroed by CTA 0 (long done in practice).
         if (ld_acquire_u64(a.zero_flag) < ctl->launch + 1) {
             const uint64_t t0 = globaltimer();
             while (ld_acquire_u64(a.zero_flag) < ctl->launch + 1) {
@@ -730,10 +722,8 @@ int launch_sf(const StreamFfnArgs &fa, cudaStream_t st) {
     cfg.stream = st;
     // programmatic dependent launch: the launch overlaps the previous
     // kernel's tail; the kernel waits for it before touching global memory.
-    // Cooperative: with several labelled tokens CTAs meet at a grid barrier,
-    // so all of them must be resident.  (Without the barrier the only
-    // cross-CTA wait is on a running CTA, the first ticket's; the launch stays
-    // cooperative there too -- measured 0.8 us faster at B = 1 than without.)
+    // Cooperative: CTAs wait for CTA 0's zeroed output (and, with several
+    // labelled tokens, for the grid barrier), so all of them must be resident.
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;

@@ -102,6 +102,7 @@ struct TcCtl {
     uint64_t xchg_free;   // partner: it has read this CTA's slot
     uint64_t ids_ready;   // epilogue: the down unit's ids are emitted
     uint32_t tmem_base;
+    int last;             // this CTA finished last: it resets the launch's counters
     volatile int abort;
 };
 
@@ -119,7 +120,9 @@ struct TcArgs {
     const float *x;              // [B][d] fp32 activations
     __half *x16;                 // [Np][d] fp16 activations (rows >= B zero), written in phase 0
     __half *h16;                 // [Np][fpad] h, K-major per token
-    uint32_t *seg_bits;          // [W] batch union, written in phase 0
+    uint32_t *seg_bits;          // [W] (unused: the union travels in tc_bits)
+    uint32_t *tc_bits;           // [W] batch union, OR-accumulated in phase 0; zero on entry, re-zeroed by
+                                 // the launch's last CTA
     const __half *bias_g, *bias_u;  // [f] fp16 gate / up biases, or null
     unsigned int *gbar;          // [3] per-launch counters: grid-barrier arrivals, CTAs whose share of
                                  // the activations / zeroed output is written, CTAs done (zero on entry;
@@ -629,29 +632,24 @@ ffn_tc_kernel(const __grid_constant__ TcMaps maps, const TcArgs a) {
         float2 xv0 = make_float2(0.f, 0.f), xv1 = make_float2(0.f, 0.f);
         if (gt < n2 && (int)((2 * gt) / a.d) < a.B) xv0 = *reinterpret_cast<const float2 *>(a.x + 2 * gt);
         if (gt + gs < n2 && (int)((2 * (gt + gs)) / a.d) < a.B) xv1 = *reinterpret_cast<const float2 *>(a.x + 2 * (gt + gs));
-        // word w is handled by CTA w % grid, so every SM shares the label reads
-        const int gwarps = gridDim.x * kTcWarps;
-        for (int w = warp * gridDim.x + blockIdx.x; w < W; w += gwarps) {
+        // Items (word w, 8-token group c), item i handled by warp i of the
+        // grid's warps taken CTA-major, so every warp of every SM keeps label
+        // loads in flight (one 128-byte row segment per token); the groups'
+        // ballots meet in tc_bits by atomic OR.
+        const int TC = (a.B + 7) >> 3;
+        const int gwarps = gridDim.x * kTcWarps, items = W * TC;
+        for (int it = warp * gridDim.x + blockIdx.x; it < items; it += gwarps) {
+            const int w = it / TC, t0 = (it - w * TC) * 8;
             const int j = w * 32 + lane;
             const bool in = j < a.f;
-            uint32_t seg = 0;
-            if (a.tok_in) {
-                for (int t = lane; t < a.B; t += 32) seg |= __ldg(a.tok_in + (int64_t)t * W + w);
-                seg = __reduce_or_sync(0xffffffffu, seg) & (w == W - 1 && (a.f & 31) ? (1u << (a.f & 31)) - 1u : ~0u);
-            } else {
-                // lane j: is neuron 32 w + j active for any token (all of a
-                // 32-token group's labels in flight at once)
-                bool any = false;
-                for (int t0 = 0; t0 < a.B; t0 += 32) {
-                    float v[32];
+            float v[8];
 #pragma unroll
-                    for (int q = 0; q < 32; ++q) v[q] = (in && t0 + q < a.B) ? __ldg(a.labels + (int64_t)(t0 + q) * a.f + j) : 0.0f;
+            for (int q = 0; q < 8; ++q) v[q] = (in && t0 + q < a.B) ? __ldg(a.labels + (int64_t)(t0 + q) * a.f + j) : 0.0f;
+            bool any = false;
 #pragma unroll
-                    for (int q = 0; q < 32; ++q) any |= v[q] > 0.0f;
-                }
-                seg = __ballot_sync(0xffffffffu, any);
-            }
-            if (lane == 0) a.seg_bits[w] = seg;
+            for (int q = 0; q < 8; ++q) any |= v[q] > 0.0f;
+            const uint32_t seg = __ballot_sync(0xffffffffu, any);
+            if (lane == 0 && seg) atomicOr(a.tc_bits + w, seg);
         }
         if (gt < n2) reinterpret_cast<__half2 *>(a.x16)[gt] = __floats2half2_rn(xv0.x, xv0.y);
         if (gt + gs < n2) reinterpret_cast<__half2 *>(a.x16)[gt + gs] = __floats2half2_rn(xv1.x, xv1.y);
@@ -679,7 +677,7 @@ ffn_tc_kernel(const __grid_constant__ TcMaps maps, const TcArgs a) {
         }
         __syncthreads();
         if (tid == 0) stamp(a, kTrBarrier);
-        for (int w = tid; w < W; w += kTcThreads) bits[w] = __ldcg(a.seg_bits + w);
+        for (int w = tid; w < W; w += kTcThreads) bits[w] = __ldcg(a.tc_bits + w);
     }
     __syncthreads();
     scan_popc(bits, W, prefix, wtot);  // ends with __syncthreads
@@ -1146,13 +1144,17 @@ ffn_tc_kernel(const __grid_constant__ TcMaps maps, const TcArgs a) {
     // has passed all its waits on them.
     if (tid == 0) {
         __threadfence();
-        if (atomicAdd(a.gbar + 2, 1u) == gridDim.x - 1) {
+        ctl->last = atomicAdd(a.gbar + 2, 1u) == gridDim.x - 1;
+        if (ctl->last) {
             for (int c = 0; c < nclu; ++c) a.ready[c] = 0u;
             a.gbar[0] = 0u;
             a.gbar[1] = 0u;
             a.gbar[2] = 0u;
         }
     }
+    __syncthreads();
+    if (ctl->last && !bits_in)
+        for (int w = tid; w < W; w += kTcThreads) a.tc_bits[w] = 0u;
     // The partner may still signal this CTA's barriers until it is done.
     cluster_sync_all();
     if (warp == kMmaWarp) {
@@ -1370,6 +1372,7 @@ int launch_ffn_tc(const TcLaunch &L, cudaStream_t st) {
     a.bias_u = L.bias_u;
     a.h16 = L.h16;
     a.seg_bits = L.seg_bits;
+    a.tc_bits = L.tc_bits;
     a.out = L.out;
     a.merge_out = L.merge_out;
     a.count_out = L.count_out;
