@@ -159,8 +159,11 @@ int spb_dequantize_rows(const void *q, int wtype, int rows, int d, float *out, v
  * 137-141, Linear(d,D) -> ReLU -> Linear(D,f), no biases) with the decision
  * sigmoid(logit) >= 0.5 (trainer_mlp.py:35-37).
  *   p1 [D][d] fp16 (fc1.weight), p2 [f][D] fp16 (fc2.weight), x [B][d] fp32
- *   hidden = fp16(ReLU(p1 . fp16(x))), logit = p2 . hidden (fp32, a fixed
- *   reduction order, so logits and index sets reproduce bit-for-bit)
+ *   hidden = fp16(ReLU(p1 . fp16(x))), logit = p2 . hidden (fp32; up to 16
+ *   tokens one fixed reduction order, so logits and index sets reproduce
+ *   bit-for-bit; larger batches run both products as tensor-core GEMMs
+ *   (cuBLASLt, fp32 accumulation), whose logits agree to fp32 rounding and
+ *   whose sets are the exact top-k of those logits)
  *   k > 0: the k largest logits per token are active (ties -> lower id);
  *   k = 0: logit >= threshold is active (threshold 0 = sigmoid >= 0.5)
  *   labels_out [B][f] fp32 (nullable): 1 active / 0 inactive -- the label format

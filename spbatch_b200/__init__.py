@@ -34,6 +34,11 @@ class SpbError(RuntimeError):
 def _load(path: str) -> C.CDLL:
     if not os.path.exists(path):
         raise SpbError(f"{path} is missing: run `python -m spbatch_b200.build`")
+    # The library uses cuBLASLt (the predictor's GEMMs for large batches).
+    # PyTorch ships its own cuBLAS / cuBLASLt pair; loading torch first makes
+    # the library bind to that already-loaded cuBLASLt (same soname) instead
+    # of loading the toolkit's copy, which torch's cuBLAS would then pick up.
+    import torch  # noqa: F401
     L = C.CDLL(path)
     _bind(L)
     return L

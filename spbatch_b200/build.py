@@ -66,7 +66,7 @@ def build(force: bool = False, verbose_ptxas: bool = False) -> str:
     dobjs = [dbg if os.path.basename(o) == "api.o" else o for o in objs]
     for lib, ob in ((LIB, objs), (DEBUG_LIB, dobjs)):
         if force or not os.path.exists(lib) or any(os.path.getmtime(o) > os.path.getmtime(lib) for o in ob):
-            subprocess.check_call([nvcc(), *ARCH, "-shared", "-o", lib, *ob, "-lcuda"])
+            subprocess.check_call([nvcc(), *ARCH, "-shared", "-o", lib, *ob, "-lcuda", "-lcublasLt"])
     return LIB
 
 

@@ -303,7 +303,8 @@ int spb_ffn_forward_bias(const void *w_gate, const void *w_up, const void *w_dow
 
 // Predictor workspace: fp16 hidden [B][D], fp32 logits [B][f], then the
 // select's scratch (PredScratch).
-static size_t predict_layout(int B, int D, int f, char *base, __half **hidden, float **logits, PredScratch *sc) {
+static size_t predict_layout(int B, int d, int D, int f, char *base, __half **hidden, float **logits,
+                             PredScratch *sc) {
     size_t off = 0;
     auto take = [&](size_t n) {
         char *p = base ? base + off : nullptr;
@@ -317,7 +318,9 @@ static size_t predict_layout(int B, int D, int f, char *base, __half **hidden, f
     char *cc = take(sizeof(uint32_t) * (size_t)B);
     char *se = take(sizeof(int2) * (size_t)B);
     char *bi = take(sizeof(uint32_t) * (size_t)B * words_of(f));
+    char *xh = B > kPredExactMaxBatch ? take(sizeof(__half) * (size_t)B * d) : nullptr;
     if (base) {
+        sc->x16 = reinterpret_cast<__half *>(xh);
         *hidden = reinterpret_cast<__half *>(h);
         *logits = reinterpret_cast<float *>(l);
         sc->hist = reinterpret_cast<uint32_t *>(hi);
@@ -329,9 +332,15 @@ static size_t predict_layout(int B, int D, int f, char *base, __half **hidden, f
     return off;
 }
 
+static size_t spb_predict_workspace_bytes_d(int B, int d, int D, int f) {
+    if (B <= 0 || d <= 0 || D <= 0 || f <= 0) return 0;
+    return predict_layout(B, d, D, f, nullptr, nullptr, nullptr, nullptr);
+}
+
 size_t spb_predict_workspace_bytes(int B, int D, int f) {
-    if (B <= 0 || D <= 0 || f <= 0) return 0;
-    return predict_layout(B, D, f, nullptr, nullptr, nullptr, nullptr);
+    // d is not known here: room for the largest activations the tensor-core
+    // route stages (d up to 16384); spb_predict checks the actual need
+    return spb_predict_workspace_bytes_d(B, 16384, D, f);
 }
 
 int spb_predict(const void *p1, const void *p2, const float *x, int B, int d, int D, int f, int k, float threshold,
@@ -341,12 +350,12 @@ int spb_predict(const void *p1, const void *p2, const float *x, int B, int d, in
     if (B <= 0 || d <= 0 || D <= 0 || f <= 0 || k < 0) return fail(SPB_ERR_INVALID, "spb_predict: bad shape");
     if (d % 256 || D % 256) return fail(SPB_ERR_INVALID, "spb_predict: d and D must be multiples of 256");
     if (!aligned16(p1) || !aligned16(p2)) return fail(SPB_ERR_INVALID, "spb_predict: weights must be 16-byte aligned");
-    const size_t need = spb_predict_workspace_bytes(B, D, f);
+    const size_t need = spb_predict_workspace_bytes_d(B, d, D, f);
     if (!workspace || workspace_bytes < need) return fail(SPB_ERR_WORKSPACE, "spb_predict: workspace too small");
     __half *hidden = nullptr;
     float *logits = nullptr;
     PredScratch sc{};
-    predict_layout(B, D, f, static_cast<char *>(workspace), &hidden, &logits, &sc);
+    predict_layout(B, d, D, f, static_cast<char *>(workspace), &hidden, &logits, &sc);
     if (logits_out) logits = logits_out;
     return launch_predict(static_cast<const __half *>(p1), static_cast<const __half *>(p2), x, B, d, D, f, k,
                           threshold, labels_out, bits_out, idx_out, count_out, logits, hidden, sc,

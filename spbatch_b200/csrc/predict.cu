@@ -17,10 +17,24 @@
 // Launches: hidden GEMV, logit GEMV (both CUDA cores, weights stream once per
 // token group), per-token exact radix select that writes the reference's
 // label format ([B][f] fp32, 1 = active) and the ascending index list.
+//
+// Batches above kPredExactMaxBatch would re-stream the weights once per
+// 8-token group on CUDA cores; they take the tensor cores instead: x is
+// rounded to fp16, hidden = fp16(ReLU(x P1^T)) and logits = hidden P2^T are
+// two cuBLASLt GEMMs (fp16 operands, fp32 accumulation, the ReLU and the fp16
+// rounding in the first GEMM's epilogue), a histogram pass bins the logits,
+// and the same selects run.  The tensor cores' summation order is not the
+// oracle's: logits agree to fp32 rounding, and the sets are the exact top-k
+// of these logits (they can differ from the oracle's where two logits lie
+// within that rounding of the k-th).
 #include "spb_internal.h"
 #include "spb_scan.cuh"
 
+#include <cublasLt.h>
+
 #include <algorithm>
+#include <mutex>
+#include <vector>
 
 namespace spb {
 
@@ -540,6 +554,90 @@ pred_gsel_b_kernel(int f, int k, uint32_t *__restrict__ bits, float *__restrict_
     }
 }
 
+// Tensor-core route: x -> fp16 (and the histograms / candidate counters zeroed).
+__global__ void __launch_bounds__(256)
+pred_prep_kernel(const float *__restrict__ x, __half *__restrict__ x16, int64_t n, uint32_t *__restrict__ hist,
+                 int B, uint32_t *__restrict__ cand_cnt) {
+    pdl_enter();
+    const int64_t gt = (int64_t)blockIdx.x * blockDim.x + threadIdx.x, gs = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = gt; i < n / 4; i += gs) {
+        const float4 v = __ldg(reinterpret_cast<const float4 *>(x) + i);
+        const __half2 h0 = __floats2half2_rn(v.x, v.y), h1 = __floats2half2_rn(v.z, v.w);
+        uint2 pk;
+        pk.x = *reinterpret_cast<const uint32_t *>(&h0);
+        pk.y = *reinterpret_cast<const uint32_t *>(&h1);
+        reinterpret_cast<uint2 *>(x16)[i] = pk;
+    }
+    if (hist)
+        for (int64_t i = gt; i < (int64_t)B * kHistBins; i += gs) hist[i] = 0u;
+    if (cand_cnt)
+        for (int64_t i = gt; i < B; i += gs) cand_cnt[i] = 0u;
+}
+
+// Per-token histograms of the logits' top 11 key bits (tensor-core route),
+// grid (ceil(f / 4096), B): a shared histogram per CTA, flushed once.
+__global__ void __launch_bounds__(256)
+pred_hist_kernel(const float *__restrict__ logits, int f, uint32_t *__restrict__ hist) {
+    __shared__ uint32_t bins[kHistBins];
+    pdl_enter();
+    const int t = blockIdx.y;
+    for (int i = threadIdx.x; i < kHistBins; i += blockDim.x) bins[i] = 0u;
+    __syncthreads();
+    const int j1 = min(f, (int)(blockIdx.x + 1) * 4096);
+    for (int j = blockIdx.x * 4096 + threadIdx.x; j < j1; j += blockDim.x)
+        atomicAdd(&bins[order_key(__ldg(logits + (int64_t)t * f + j)) >> 21], 1u);
+    __syncthreads();
+    for (int i = threadIdx.x; i < kHistBins; i += blockDim.x)
+        if (bins[i]) atomicAdd(hist + (int64_t)t * kHistBins + i, bins[i]);
+}
+
+namespace {
+
+cublasLtHandle_t lt_handle() {
+    static std::mutex mu;
+    static std::vector<cublasLtHandle_t> handles;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lk(mu);
+    if ((int)handles.size() <= dev) handles.resize(dev + 1, nullptr);
+    if (!handles[dev] && cublasLtCreate(&handles[dev]) != CUBLAS_STATUS_SUCCESS) handles[dev] = nullptr;
+    return handles[dev];
+}
+
+// C[n][m] (row-major, m contiguous) = op(A[m][K] row-major) . B[n][K]^T in
+// column-major terms: C (m x n, ld m) = A^T (A stored K x m, ld K) . B (K x n, ld K).
+// fp16 A and B, fp32 accumulation; C fp16 with ReLU, or fp32.
+int lt_gemm(const __half *a, const __half *b, void *c, int m, int n, int K, bool relu_fp16, cudaStream_t st) {
+    cublasLtHandle_t h = lt_handle();
+    if (!h) return fail(SPB_ERR_CUDA, "spb_predict: cublasLtCreate failed");
+    cublasLtMatmulDesc_t op = nullptr;
+    cublasLtMatrixLayout_t la = nullptr, lb = nullptr, lc = nullptr;
+    int rc = SPB_OK;
+    const cublasOperation_t tA = CUBLAS_OP_T, tB = CUBLAS_OP_N;
+    const cublasLtEpilogue_t epi = relu_fp16 ? CUBLASLT_EPILOGUE_RELU : CUBLASLT_EPILOGUE_DEFAULT;
+    const cudaDataType_t ct = relu_fp16 ? CUDA_R_16F : CUDA_R_32F;
+    const float alpha = 1.0f, beta = 0.0f;
+    if (cublasLtMatmulDescCreate(&op, CUBLAS_COMPUTE_32F, CUDA_R_32F) != CUBLAS_STATUS_SUCCESS ||
+        cublasLtMatmulDescSetAttribute(op, CUBLASLT_MATMUL_DESC_TRANSA, &tA, sizeof(tA)) != CUBLAS_STATUS_SUCCESS ||
+        cublasLtMatmulDescSetAttribute(op, CUBLASLT_MATMUL_DESC_TRANSB, &tB, sizeof(tB)) != CUBLAS_STATUS_SUCCESS ||
+        cublasLtMatmulDescSetAttribute(op, CUBLASLT_MATMUL_DESC_EPILOGUE, &epi, sizeof(epi)) != CUBLAS_STATUS_SUCCESS ||
+        cublasLtMatrixLayoutCreate(&la, CUDA_R_16F, K, m, K) != CUBLAS_STATUS_SUCCESS ||
+        cublasLtMatrixLayoutCreate(&lb, CUDA_R_16F, K, n, K) != CUBLAS_STATUS_SUCCESS ||
+        cublasLtMatrixLayoutCreate(&lc, ct, m, n, m) != CUBLAS_STATUS_SUCCESS) {
+        rc = fail(SPB_ERR_CUDA, "spb_predict: cublasLt descriptors");
+    } else if (cublasLtMatmul(h, op, &alpha, a, la, b, lb, &beta, c, lc, c, lc, nullptr, nullptr, 0, st) !=
+               CUBLAS_STATUS_SUCCESS) {
+        rc = fail(SPB_ERR_CUDA, "spb_predict: cublasLtMatmul failed");
+    }
+    if (lc) cublasLtMatrixLayoutDestroy(lc);
+    if (lb) cublasLtMatrixLayoutDestroy(lb);
+    if (la) cublasLtMatrixLayoutDestroy(la);
+    if (op) cublasLtMatmulDescDestroy(op);
+    return rc;
+}
+
+}  // namespace
+
 int launch_predict(const __half *p1, const __half *p2, const float *x, int B, int d, int D, int f, int k,
                    float threshold, float *labels, uint32_t *bits, int32_t *idx, int32_t *counts, float *logits,
                    __half *hidden, const PredScratch &sc, cudaStream_t st) {
@@ -548,42 +646,57 @@ int launch_predict(const __half *p1, const __half *p2, const float *x, int B, in
     // sets without an index list: the grid-wide select
     const bool grid_sel = hist && !idx;
     const int sms = num_sms();
-    {
-        // 8 tokens beyond B = 1: wider groups make the CUDA-core loop
-        // shared-memory and FMA bound (measured slower at B = 32 / 64)
-        const int NTH = B == 1 ? 1 : 8;
-        const int ty = (B + NTH - 1) / NTH;
-        // one row per warp when that fills the GPU: every row's loads are in
-        // flight at once (each warp's 8 KB row is the fixed-order dot unit)
-        const int ctas = max(1, (2 * sms + ty - 1) / ty);
-        const int rows = std::min((D + ctas - 1) / ctas, kPredWarps);
-        const size_t smem = sizeof(__half) * NTH * d;
-        if (smem > 200 * 1024) return fail(SPB_ERR_UNSUPPORTED, "spb_predict: d too large");
-        const bool kb16 = d / 8 >= 32 * 16;
-        auto kern = NTH == 1 ? (kb16 ? pred_hidden_kernel<1, 16> : pred_hidden_kernel<1, 8>)
-                  : NTH == 8 ? (kb16 ? pred_hidden_kernel<8, 16> : pred_hidden_kernel<8, 8>)
-                             : (kb16 ? pred_hidden_kernel<8, 16> : pred_hidden_kernel<8, 8>);
-        if (int rc = ensure_smem((const void *)kern, smem)) return rc;
-        if (int rc = launch_pdl(kern, dim3((D + rows - 1) / rows, ty), dim3(kPredThreads), smem, st,
-                                "pred_hidden_kernel", p1, x, hidden, B, d, D, rows, hist,
+    if (B > kPredExactMaxBatch) {
+        // tensor-core route: x16, two GEMMs, histograms
+        const int64_t n = (int64_t)B * d;
+        if (int rc = launch_pdl(pred_prep_kernel, dim3(std::max(1, std::min(2 * sms, (int)((n / 4 + 255) / 256)))),
+                                dim3(256), 0, st, "pred_prep_kernel", x, sc.x16, n, hist, B,
                                 grid_sel ? sc.cand_cnt : nullptr))
             return rc;
-    }
-    {
-        // at most four rows per warp: rows of D = 1024 are only 2 KB, so a
-        // warp walking many of them in turn is latency-bound; more CTAs keep
-        // more rows in flight (each CTA re-stages NT x D fp16 from L2)
-        const int NTL = B == 1 ? 1 : 8;
-        const int ty = (B + NTL - 1) / NTL;
-        const int ctas = max(1, (4 * sms + ty - 1) / ty);
-        const int rows = std::min((f + ctas - 1) / ctas, 4 * kPredWarps);
-        const size_t smem = sizeof(__half) * NTL * D;
-        if (smem > 200 * 1024) return fail(SPB_ERR_UNSUPPORTED, "spb_predict: D too large");
-        auto kern = NTL == 1 ? pred_logit_kernel<1> : pred_logit_kernel<8>;
-        if (int rc = ensure_smem((const void *)kern, smem)) return rc;
-        if (int rc = launch_pdl(kern, dim3((f + rows - 1) / rows, ty), dim3(kPredThreads), smem, st,
-                                "pred_logit_kernel", p2, hidden, logits, B, D, f, rows, hist))
-            return rc;
+        if (int rc = lt_gemm(p1, sc.x16, hidden, D, B, d, true, st)) return rc;
+        if (int rc = lt_gemm(p2, hidden, logits, f, B, D, false, st)) return rc;
+        if (hist)
+            if (int rc = launch_pdl(pred_hist_kernel, dim3((f + 4095) / 4096, B), dim3(256), 0, st,
+                                    "pred_hist_kernel", (const float *)logits, f, hist))
+                return rc;
+    } else {
+        {
+            // 8 tokens beyond B = 1: wider groups make the CUDA-core loop
+            // shared-memory and FMA bound (measured slower at B = 32 / 64)
+            const int NTH = B == 1 ? 1 : 8;
+            const int ty = (B + NTH - 1) / NTH;
+            // one row per warp when that fills the GPU: every row's loads are in
+            // flight at once (each warp's 8 KB row is the fixed-order dot unit)
+            const int ctas = max(1, (2 * sms + ty - 1) / ty);
+            const int rows = std::min((D + ctas - 1) / ctas, kPredWarps);
+            const size_t smem = sizeof(__half) * NTH * d;
+            if (smem > 200 * 1024) return fail(SPB_ERR_UNSUPPORTED, "spb_predict: d too large");
+            const bool kb16 = d / 8 >= 32 * 16;
+            auto kern = NTH == 1 ? (kb16 ? pred_hidden_kernel<1, 16> : pred_hidden_kernel<1, 8>)
+                      : NTH == 8 ? (kb16 ? pred_hidden_kernel<8, 16> : pred_hidden_kernel<8, 8>)
+                                 : (kb16 ? pred_hidden_kernel<8, 16> : pred_hidden_kernel<8, 8>);
+            if (int rc = ensure_smem((const void *)kern, smem)) return rc;
+            if (int rc = launch_pdl(kern, dim3((D + rows - 1) / rows, ty), dim3(kPredThreads), smem, st,
+                                    "pred_hidden_kernel", p1, x, hidden, B, d, D, rows, hist,
+                                    grid_sel ? sc.cand_cnt : nullptr))
+                return rc;
+        }
+        {
+            // at most four rows per warp: rows of D = 1024 are only 2 KB, so a
+            // warp walking many of them in turn is latency-bound; more CTAs keep
+            // more rows in flight (each CTA re-stages NT x D fp16 from L2)
+            const int NTL = B == 1 ? 1 : 8;
+            const int ty = (B + NTL - 1) / NTL;
+            const int ctas = max(1, (4 * sms + ty - 1) / ty);
+            const int rows = std::min((f + ctas - 1) / ctas, 4 * kPredWarps);
+            const size_t smem = sizeof(__half) * NTL * D;
+            if (smem > 200 * 1024) return fail(SPB_ERR_UNSUPPORTED, "spb_predict: D too large");
+            auto kern = NTL == 1 ? pred_logit_kernel<1> : pred_logit_kernel<8>;
+            if (int rc = ensure_smem((const void *)kern, smem)) return rc;
+            if (int rc = launch_pdl(kern, dim3((f + rows - 1) / rows, ty), dim3(kPredThreads), smem, st,
+                                    "pred_logit_kernel", p2, hidden, logits, B, D, f, rows, hist))
+                return rc;
+        }
     }
     if (grid_sel) {
         uint32_t *wb = bits ? bits : sc.bits;

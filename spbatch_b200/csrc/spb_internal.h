@@ -123,12 +123,18 @@ const DebugHooks &debug_hooks();
 
 // predict.cu -- low-rank activity predictor
 // predictor scratch inside the caller's workspace
+// Batches above this size take the predictor's tensor-core route (fp16 GEMMs
+// with fp32 accumulation); up to it the CUDA-core kernels with one fixed
+// summation order (logits and sets bit-exact against the oracle).
+constexpr int kPredExactMaxBatch = 16;
+
 struct PredScratch {
     uint32_t *hist;      // [B][2048] logit histograms (top 11 key bits)
     uint2 *cand;         // [B][f] (key, id) candidates of the threshold bin
     uint32_t *cand_cnt;  // [B]
     int2 *sel;           // [B] threshold bin, keys still needed from it
     uint32_t *bits;      // [B][W] set words when the caller wants labels only
+    __half *x16;         // [B][d] fp16 activations (tensor-core route, B > kPredExactMaxBatch)
 };
 int launch_predict(const __half *p1, const __half *p2, const float *x, int B, int d, int D, int f, int k,
                    float threshold, float *labels, uint32_t *bits, int32_t *idx, int32_t *counts, float *logits,
