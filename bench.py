@@ -106,6 +106,14 @@ def hbm_peak():
         return FALLBACK_HBM_GBS, "fallback"
 
 
+def pred_launches(B):
+    """Kernels of this library that spb_predict launches for set words (top-k,
+    no index list): one fused launch at B = 1; hidden, logit and two selects
+    up to 16 tokens; above, x -> fp16, a histogram pass and two selects around
+    two cuBLASLt GEMMs."""
+    return 1 if B == 1 else 4
+
+
 def workload_name(a, U, B=None):
     wt = {"f16": "fp16 weights", "q8_0": "Q8_0 weights", "q4_0": "Q4_0 weights"}[a.wtype]
     act = (f"{a.activity:.0%} per-token activity from the DejaVu predictor (top-k, run ahead of the layer)"
@@ -330,6 +338,9 @@ def run_ours(a):
             for ly in layers:
                 ly["lab_np"] = ly["lab"].cpu().numpy()
                 ly["U"] = ly["U_full"] = int((ly["lab_np"] > 0).any(0).sum())
+                # the timed step passes the sets as bit words (spb_predict ->
+                # spb_ffn_forward_bits), no [B][f] label matrix in between
+                ly["bits"] = torch.zeros((B, (f1 - f0 + 31) // 32), dtype=torch.int32, device=device)
 
         def fwd(i, x=None, lab=None, out=None):
             ly = layers[i]
@@ -337,9 +348,12 @@ def run_ours(a):
             ll = ly["lab"] if lab is None else lab
             o = ly["out"] if out is None else out
             if a.predictor:
-                spb.predict(P[i][0], P[i][1], xx, k=k, out=ll, workspace=pw)
-            spb.ffn_forward(*Wl[i], xx, ll, wtype=wtype, out=o, per_token_mask=bool(a.per_token), path=path,
-                            workspace=ws)
+                spb.predict(P[i][0], P[i][1], xx, k=k, bits_out=ly["bits"], labels=False, workspace=pw)
+                spb.ffn_forward(*Wl[i], xx, bits=ly["bits"], f=f1 - f0, wtype=wtype, out=o,
+                                per_token_mask=bool(a.per_token), path=path, workspace=ws)
+            else:
+                spb.ffn_forward(*Wl[i], xx, ll, wtype=wtype, out=o, per_token_mask=bool(a.per_token), path=path,
+                                workspace=ws)
             if sharded:  # one all-reduce of the [B][d] partial outputs (NCCL)
                 dist.all_reduce(o)
 
@@ -443,7 +457,7 @@ def run_ours(a):
         "clocks": head["clocks"],
         "timing": {"repeats": head["reps"], "ms_per_step_samples": [round(s, 5) for s in head["samples"]],
                    "statistic": "median over repeats of the K-step region"},
-        "gpu_launches": int(spb.lib().spb_ffn_launches(a.batch, d, wtype, path) + (3 if a.predictor else 0)) * K,
+        "gpu_launches": int(spb.lib().spb_ffn_launches(a.batch, d, wtype, path) + (pred_launches(a.batch) if a.predictor else 0)) * K,
     }
     if sharded:
         rec["shard_parity"] = shard_parity

@@ -29,6 +29,7 @@
 // within that rounding of the k-th).
 #include "spb_internal.h"
 #include "spb_scan.cuh"
+#include "tc_ptx.cuh"
 
 #include <cublasLt.h>
 
@@ -37,6 +38,22 @@
 #include <vector>
 
 namespace spb {
+
+using namespace ptx;
+
+// Mixed-precision FMA (sm_100): fp16 operands, fp32 addend and result, one
+// rounding -- the value fmaf((float)a, (float)b, c) gives, without the two
+// conversions.  fma2_lohi adds the low pair, then the high pair.
+__device__ __forceinline__ float fma2_lohi(uint32_t a, uint32_t b, float c) {
+    asm("{\n\t.reg .f16 al, ah, bl, bh;\n\t"
+        "mov.b32 {al, ah}, %1;\n\t"
+        "mov.b32 {bl, bh}, %2;\n\t"
+        "fma.rn.f32.f16 %0, al, bl, %0;\n\t"
+        "fma.rn.f32.f16 %0, ah, bh, %0;\n\t}"
+        : "+f"(c)
+        : "r"(a), "r"(b));
+    return c;
+}
 
 constexpr int kPredThreads = 256;
 constexpr int kPredWarps = kPredThreads / 32;
@@ -64,30 +81,16 @@ __device__ __forceinline__ void fixed_dot(const __half *__restrict__ row, const 
             const int c = c0 + u * 32;
             if (c >= nch) break;
             const uint32_t *pw = reinterpret_cast<const uint32_t *>(&wv[u]);
-            float w[8];
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                const float2 f2 = h2f2(pw[q]);
-                w[2 * q] = f2.x;
-                w[2 * q + 1] = f2.y;
-            }
 #pragma unroll
             for (int t = 0; t < NT; ++t) {
                 if (t < nt) {
                     // the staged vector holds fp16 values (exact: x and hidden
                     // are fp16-rounded): one conflict-free 16-byte load per
-                    // chunk, converted exactly; same FMA order
+                    // chunk; elements in order, fp16 x fp16 + fp32
                     const uint4 hv = *reinterpret_cast<const uint4 *>(vs + (int64_t)t * n + c * 8);
                     const uint32_t *ph = reinterpret_cast<const uint32_t *>(&hv);
-                    float ve[8];
 #pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        const float2 f2 = h2f2(ph[q]);
-                        ve[2 * q] = f2.x;
-                        ve[2 * q + 1] = f2.y;
-                    }
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) acc[t] = fmaf(w[e], ve[e], acc[t]);
+                    for (int q = 0; q < 4; ++q) acc[t] = fma2_lohi(pw[q], ph[q], acc[t]);
                 }
             }
         }
@@ -554,6 +557,287 @@ pred_gsel_b_kernel(int f, int k, uint32_t *__restrict__ bits, float *__restrict_
     }
 }
 
+// ---- one-launch predictor for one token (top-k into set words) ------------
+//
+// At B = 1 the four-launch chain above spends most of its time in launch
+// ramps and in the two select launches.  This kernel does the whole
+// predictor in one cooperative launch of one CTA per SM:
+//   A. Warps kPfHidW.. copy the CTA's contiguous slice of P2 rows [j0, j1)
+//      into shared memory with 16-byte cp.async (P2 is not written by the
+//      previous kernel, so the copies start before the dependency wait).
+//   B. Warps 0..kPfHidW-1 stage x as fp16 and compute the CTA's share of
+//      hidden = fp16(ReLU(P1 x)) (warp per row, the chain's fixed-order dot),
+//      zero the histogram and set words, then meet the grid at a barrier.
+//   C. Logits of the slice from shared memory with the same fixed order
+//      (bit-identical to pred_logit_kernel), kept as order keys and written
+//      out; the keys are binned in shared memory and the non-zero bins added
+//      to the global 11-bit histogram.
+//   D. Grid barrier; every CTA reads the histogram and all logits (L2) in one
+//      round trip, finds the threshold bin and how many keys it still needs
+//      from it, compacts that bin's candidates in id order (block scan), and
+//      decides its own rows: above the bin, or in it with rank < need (rank =
+//      candidates with a larger key, or an equal key and a lower id) -- the
+//      exact top-k with ties to the lower id.
+// Grid barriers use a monotonic counter in this module's device memory:
+// every CTA arrives at both barriers of every launch, so arrival counts stay
+// multiples of the grid, and launches of this full-device grid do not overlap.
+constexpr int kPfThreads = 512;
+constexpr int kPfWarps = kPfThreads / 32;
+constexpr int kPfHidW = 8;  // warps computing hidden rows; the others copy the P2 slice
+constexpr uint64_t kPfTimeoutNs = 2000000000ull;
+__device__ unsigned long long g_pf_arrivals;
+
+__device__ __forceinline__ void pf_block_sync(int nthreads) {
+    if (nthreads == (int)blockDim.x) __syncthreads();
+    else asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
+}
+
+// Grid barrier for the first nthreads threads (whole warps) of every CTA
+// (cooperative launch: every CTA is resident).  Bounded: a barrier that
+// never completes sets *fail and the launch finishes.
+__device__ __forceinline__ void pf_grid_sync(int *fail, int nthreads) {
+    pf_block_sync(nthreads);
+    if (threadIdx.x == 0) {
+        unsigned long long ticket;
+        __threadfence();
+        asm volatile("atom.add.release.gpu.global.u64 %0, [%1], 1;" : "=l"(ticket) : "l"(&g_pf_arrivals) : "memory");
+        const unsigned long long target = (ticket / gridDim.x + 1) * gridDim.x;
+        const uint64_t t0 = globaltimer();
+        for (;;) {
+            unsigned long long v;
+            asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(&g_pf_arrivals) : "memory");
+            if (v >= target) break;
+            if (globaltimer() - t0 > kPfTimeoutNs) {
+                *fail = 1;
+                break;
+            }
+            __nanosleep(64);
+        }
+    }
+    pf_block_sync(nthreads);
+}
+
+// Fixed-order dot of R shared-memory rows (rows, rows + n, ...) with one
+// shared-memory vector: the order of fixed_dot per row (lane l takes the
+// 8-element chunks l, l + 32, ... in turn, elements in order, then the xor
+// butterfly), the rows' FMA chains interleaved.
+template <int R>
+__device__ __forceinline__ void fixed_dot_smem_rows(const __half *rows, const __half *v, int n, float (&acc)[R]) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int r = 0; r < R; ++r) acc[r] = 0.0f;
+    const int nch = n / 8;
+    for (int c = lane; c < nch; c += 32) {
+        const uint4 hv = *reinterpret_cast<const uint4 *>(v + c * 8);
+        const uint32_t *ph = reinterpret_cast<const uint32_t *>(&hv);
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            const uint4 wv = *reinterpret_cast<const uint4 *>(rows + (size_t)r * n + c * 8);
+            const uint32_t *pw = reinterpret_cast<const uint32_t *>(&wv);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) acc[r] = fma2_lohi(pw[q], ph[q], acc[r]);
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], o);
+    }
+}
+
+// Shared memory: xs [d] | hs [D] | keys [rows] | shist [2048] |
+// P2 slice [rows][D] (reused in D: candidates [f], logits [f]).
+template <int KB>
+__global__ void __launch_bounds__(kPfThreads, 1)
+pred_fused_kernel(const __half *__restrict__ p1, const __half *__restrict__ p2, const float *__restrict__ x, int d,
+                  int D, int f, int k, int rows, __half *__restrict__ hidden, float *__restrict__ logits,
+                  uint32_t *__restrict__ hist, uint32_t *__restrict__ bits, float *__restrict__ labels,
+                  int32_t *__restrict__ counts) {
+    extern __shared__ __align__(16) uint8_t pf_smem[];
+    __half *xs = reinterpret_cast<__half *>(pf_smem);
+    __half *hs = xs + d;
+    uint32_t *keys = reinterpret_cast<uint32_t *>(hs + D);
+    uint32_t *shist = keys + ((rows + 3) & ~3);
+    __half *p2s = reinterpret_cast<__half *>(shist + kHistBins);
+    uint2 *cand = reinterpret_cast<uint2 *>(p2s);     // [f] candidates (phase D)
+    float *lgs = reinterpret_cast<float *>(cand + f);  // [f] logits (phase D)
+    __shared__ int s_fail, s_nc, s_need;
+    __shared__ uint32_t s_bin;
+    __shared__ int warp_tot[kPfWarps + 1];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int G = gridDim.x, W = (f + 31) / 32;
+    const int j0 = min(f, (int)blockIdx.x * rows), nrow = min(f, j0 + rows) - j0;
+    constexpr int kHidT = kPfHidW * 32;
+    if (tid == 0) s_fail = 0;
+    // ---- A / B ----
+    if (warp >= kPfHidW) {
+        const uint32_t dst = (uint32_t)__cvta_generic_to_shared(p2s);
+        const char *src = reinterpret_cast<const char *>(p2 + (size_t)j0 * D);
+        const int n16 = nrow * D / 8;  // 16-byte pieces of the slice
+        for (int i = tid - kHidT; i < n16; i += kPfThreads - kHidT) cp_async16_full(dst + i * 16, src + (size_t)i * 16);
+        cp_async_commit();
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        cp_async_wait_all();
+    } else {
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        for (int i = tid; i < d / 4; i += kHidT) {
+            const float4 v = __ldg(reinterpret_cast<const float4 *>(x) + i);
+            const __half2 h0 = __floats2half2_rn(v.x, v.y), h1 = __floats2half2_rn(v.z, v.w);
+            uint2 pk;
+            pk.x = *reinterpret_cast<const uint32_t *>(&h0);
+            pk.y = *reinterpret_cast<const uint32_t *>(&h1);
+            reinterpret_cast<uint2 *>(xs)[i] = pk;
+        }
+        for (int i = blockIdx.x * kHidT + tid; i < kHistBins; i += G * kHidT) hist[i] = 0u;
+        for (int i = blockIdx.x * kHidT + tid; i < W; i += G * kHidT) bits[i] = 0u;
+        pf_block_sync(kHidT);
+        const int hr = (D + G - 1) / G;
+        for (int r = blockIdx.x * hr + warp; r < min(D, (int)(blockIdx.x + 1) * hr); r += kPfHidW) {
+            float acc[1];
+            fixed_dot<1, KB>(p1 + (int64_t)r * d, xs, d, 1, acc);
+            if (lane == 0) hidden[r] = __float2half_rn(fmaxf(acc[0], 0.0f));
+        }
+        pf_grid_sync(&s_fail, kHidT);
+        for (int i = tid; i < D / 8; i += kHidT)
+            reinterpret_cast<uint4 *>(hs)[i] = __ldcg(reinterpret_cast<const uint4 *>(hidden) + i);
+    }
+    __syncthreads();
+    // ---- C. logits of the slice, four rows per warp at a time ----
+    {
+        constexpr int R = 4;
+        const int nfull = nrow / R * R;
+        for (int r = warp * R; r < nfull; r += kPfWarps * R) {
+            float acc[R];
+            fixed_dot_smem_rows<R>(p2s + (size_t)r * D, hs, D, acc);
+            if (lane < R) {
+                float v = acc[0];
+#pragma unroll
+                for (int q = 1; q < R; ++q)
+                    if (lane == q) v = acc[q];
+                logits[j0 + r + lane] = v;
+                keys[r + lane] = order_key(v);
+            }
+        }
+        for (int r = nfull + warp; r < nrow; r += kPfWarps) {
+            float acc[1];
+            fixed_dot_smem_rows<1>(p2s + (size_t)r * D, hs, D, acc);
+            if (lane == 0) {
+                logits[j0 + r] = acc[0];
+                keys[r] = order_key(acc[0]);
+            }
+        }
+    }
+    for (int i = tid; i < kHistBins; i += kPfThreads) shist[i] = 0u;
+    __syncthreads();
+    for (int r = tid; r < nrow; r += kPfThreads) atomicAdd(&shist[keys[r] >> 21], 1u);
+    __syncthreads();
+    for (int i = tid; i < kHistBins; i += kPfThreads)
+        if (shist[i]) atomicAdd(hist + i, shist[i]);
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    pf_grid_sync(&s_fail, kPfThreads);
+    // ---- D. the exact top-k, each CTA deciding its own rows ----
+    // One round trip: the histogram (thread i: bins 2047 - 4i .. 2044 - 4i,
+    // descending) and all logits (L2) into shared memory.
+    uint32_t c4[4], sum = 0;
+    {
+        constexpr int U = 8;
+        const bool vec = (f & 3) == 0;
+        const int n4 = vec ? f >> 2 : 0;
+        float4 v[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int i = tid + u * kPfThreads;
+            v[u] = i < n4 ? __ldcg(reinterpret_cast<const float4 *>(logits) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) c4[q] = __ldcg(hist + kHistBins - 1 - 4 * tid - q);
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int i = tid + u * kPfThreads;
+            if (i < n4) reinterpret_cast<float4 *>(lgs)[i] = v[u];
+        }
+        for (int i = tid + U * kPfThreads; i < n4; i += kPfThreads)
+            reinterpret_cast<float4 *>(lgs)[i] = __ldcg(reinterpret_cast<const float4 *>(logits) + i);
+        if (!vec)
+            for (int j = tid; j < f; j += kPfThreads) lgs[j] = __ldcg(logits + j);
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) sum += c4[q];
+    const int incl = warp_incl_scan((int)sum);
+    if (lane == 31) warp_tot[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+        const int v = lane < kPfWarps ? warp_tot[lane] : 0;
+        const int vi = warp_incl_scan(v);
+        if (lane < kPfWarps) warp_tot[lane] = vi - v;
+    }
+    __syncthreads();
+    int before = warp_tot[warp] + incl - (int)sum;  // keys in bins above this thread's
+    if (before < k && k <= before + (int)sum) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            if (before < k && k <= before + (int)c4[q]) {
+                s_bin = kHistBins - 1 - 4 * tid - q;
+                s_need = k - before;
+            }
+            before += c4[q];
+        }
+    }
+    __syncthreads();
+    const uint32_t bin = s_bin;
+    // candidates (keys in the threshold bin) compacted in id order: each
+    // thread counts its contiguous run, one block scan places them
+    const int per = (f + kPfThreads - 1) / kPfThreads;
+    const int ja = min(f, tid * per), jb = min(f, ja + per);
+    int mine = 0;
+    for (int j = ja; j < jb; ++j) mine += (order_key(lgs[j]) >> 21) == bin;
+    const int mi = warp_incl_scan(mine);
+    if (lane == 31) warp_tot[warp] = mi;
+    __syncthreads();
+    if (warp == 0) {
+        const int v = lane < kPfWarps ? warp_tot[lane] : 0;
+        const int vi = warp_incl_scan(v);
+        if (lane < kPfWarps) warp_tot[lane] = vi - v;
+        if (lane == kPfWarps - 1) s_nc = vi;
+    }
+    __syncthreads();
+    {
+        int pos = warp_tot[warp] + mi - mine;
+        for (int j = ja; j < jb; ++j) {
+            const uint32_t key = order_key(lgs[j]);
+            if ((key >> 21) == bin) cand[pos++] = make_uint2(key, (uint32_t)j);
+        }
+    }
+    __syncthreads();
+    const int nc = s_nc, need = s_need;
+    // own rows, a warp per 32 rows: above the bin, or ranked among the
+    // candidates (rank = larger keys, or equal keys with lower ids)
+    for (int r0 = warp * 32; r0 < nrow; r0 += kPfWarps * 32) {
+        const int r = r0 + lane;
+        const uint32_t key = r < nrow ? keys[r] : 0u;
+        const uint32_t j = (uint32_t)(j0 + r);
+        bool on = r < nrow && (key >> 21) > bin;
+        uint32_t inbin = __ballot_sync(0xffffffffu, r < nrow && (key >> 21) == bin);
+        while (inbin) {  // the warp ranks each in-bin row together
+            const int src = __ffs(inbin) - 1;
+            inbin &= inbin - 1;
+            const uint32_t kk = __shfl_sync(0xffffffffu, key, src);
+            const uint32_t jj = __shfl_sync(0xffffffffu, j, src);
+            int rank = 0;
+            for (int q = lane; q < nc; q += 32) {
+                const uint2 o = cand[q];
+                rank += o.x > kk || (o.x == kk && o.y < jj);
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) rank += __shfl_xor_sync(0xffffffffu, rank, o);
+            if (lane == src) on = rank < need;
+        }
+        if (on) atomicOr(bits + (j >> 5), 1u << (j & 31));
+        if (labels && r < nrow) labels[j] = on ? 1.0f : 0.0f;
+    }
+    if (counts && blockIdx.x == 0 && tid == 0) counts[0] = s_fail ? -1 : k;
+}
+
 // Tensor-core route: x -> fp16 (and the histograms / candidate counters zeroed).
 __global__ void __launch_bounds__(256)
 pred_prep_kernel(const float *__restrict__ x, __half *__restrict__ x16, int64_t n, uint32_t *__restrict__ hist,
@@ -646,6 +930,36 @@ int launch_predict(const __half *p1, const __half *p2, const float *x, int B, in
     // sets without an index list: the grid-wide select
     const bool grid_sel = hist && !idx;
     const int sms = num_sms();
+    if (grid_sel && B == 1 && d % 256 == 0) {
+        // one launch: P2 slices resident in shared memory, select in the tail
+        const int G = sms;
+        const int rows = (f + G - 1) / G;
+        const size_t slice = std::max(sizeof(__half) * (size_t)rows * D, (sizeof(uint2) + sizeof(float)) * (size_t)f);
+        const size_t smem =
+            sizeof(__half) * (size_t)(d + D) + sizeof(uint32_t) * ((size_t)((rows + 3) & ~3) + kHistBins) + slice;
+        if (smem <= 220 * 1024) {
+            auto kern = d / 8 >= 32 * 16 ? pred_fused_kernel<16> : pred_fused_kernel<8>;
+            if (int rc = ensure_smem((const void *)kern, smem)) return rc;
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3(G);
+            cfg.blockDim = dim3(kPfThreads);
+            cfg.dynamicSmemBytes = smem;
+            cfg.stream = st;
+            cudaLaunchAttribute attr[2];
+            attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+            attr[0].val.programmaticStreamSerializationAllowed = 1;
+            // the grid barriers need every CTA resident
+            attr[1].id = cudaLaunchAttributeCooperative;
+            attr[1].val.cooperative = 1;
+            cfg.attrs = attr;
+            cfg.numAttrs = 2;
+            uint32_t *wb = bits ? bits : sc.bits;
+            const cudaError_t e =
+                cudaLaunchKernelEx(&cfg, kern, p1, p2, x, d, D, f, k, rows, hidden, logits, hist, wb, labels, counts);
+            if (e != cudaSuccess) return cuda_fail(e, "pred_fused_kernel");
+            return SPB_OK;
+        }
+    }
     if (B > kPredExactMaxBatch) {
         // tensor-core route: x16, two GEMMs, histograms
         const int64_t n = (int64_t)B * d;

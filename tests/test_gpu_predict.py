@@ -164,3 +164,41 @@ def test_grid_select_sets_bit_exact(spb, cuda, oracle_mod, B, d, D, f, k, ties):
         np.testing.assert_array_equal(labels.cpu().numpy(), lab_ref, err_msg=f"labels, call {call}")
         np.testing.assert_array_equal(bits.cpu().numpy().view(np.uint32), _to_words(lab_ref), err_msg="bits")
         np.testing.assert_array_equal(bits_only.cpu().numpy().view(np.uint32), _to_words(lab_ref), err_msg="bits")
+
+
+@pytest.mark.parametrize("B,d,D,f,k,ties", [(1, 4096, 1024, 11008, 1101, "none"), (3, 1024, 512, 4096, 400, "none"),
+                                            (1, 512, 256, 512, 37, "some"), (1, 512, 256, 2048, 100, "all"),
+                                            (1, 5120, 1024, 13824, 1106, "none"), (1, 1024, 256, 1000, 97, "none")])
+def test_set_outputs_without_index_list(spb, cuda, oracle_mod, B, d, D, f, k, ties):
+    """Set outputs with no index list: at one token the one-launch predictor
+    (P2 slices resident in shared memory, exact top-k in the same launch),
+    otherwise the launch chain.  Logits, labels, bit words and counts
+    bit-exact against the oracle, on two calls in a row, including a row
+    where every logit ties (the k lowest ids win) and slices that f does
+    not divide evenly."""
+    import torch
+    rng = np.random.default_rng(B * 13 + f)
+    p1, p2 = _weights(rng, d, D, f)
+    if ties == "some":
+        p2[100:200] = p2[5]
+    elif ties == "all":
+        p2[:] = p2[0]
+    P1, P2 = _dev(p1, cuda), _dev(p2, cuda)
+    ws = spb.predict_workspace(B, D, f, cuda)
+    for call in range(2):
+        x = rng.standard_normal((B, d)).astype(np.float32)
+        lg_ref, lab_ref, _, cnt_ref = oracle_mod.predict(p1, p2, x, k=k)
+        X = _dev(x, cuda)
+        labels = torch.full((B, f), -1.0, device=cuda)
+        bits = torch.full((B, (f + 31) // 32), -1, dtype=torch.int32, device=cuda)
+        counts = torch.zeros(B, dtype=torch.int32, device=cuda)
+        logits = torch.empty((B, f), device=cuda)
+        rc = spb.lib().spb_predict(P1.data_ptr(), P2.data_ptr(), X.data_ptr(), B, d, D, f, k, 0.0,
+                                   labels.data_ptr(), bits.data_ptr(), None, counts.data_ptr(), logits.data_ptr(),
+                                   ws.data_ptr(), ws.numel(), torch.cuda.current_stream().cuda_stream)
+        assert rc == 0, spb.lib().spb_last_error()
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(logits.cpu().numpy(), lg_ref, err_msg=f"logits, call {call}")
+        np.testing.assert_array_equal(labels.cpu().numpy(), lab_ref, err_msg=f"labels, call {call}")
+        np.testing.assert_array_equal(bits.cpu().numpy().view(np.uint32), _to_words(lab_ref), err_msg="bits")
+        np.testing.assert_array_equal(counts.cpu().numpy(), cnt_ref, err_msg="counts")
