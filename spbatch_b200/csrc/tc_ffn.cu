@@ -90,6 +90,12 @@ enum : uint32_t {
     kErrLaunchShape = 7,   // launched without 2-CTA clusters or with an odd grid
 };
 
+constexpr int kMaxStagingSlots = 7;
+// Quantised weights: the first kQCopyThreads producer threads copy raw blocks
+// into the staging slots, the others expand landed slots into the ring.
+constexpr int kQCopyThreads = 128;
+constexpr int kQExpThreads = kProducerThreads - kQCopyThreads;
+
 struct TcCtl {
     // one of each per ring unit; every occupancy of a unit completes one
     // phase of all three (units past a stage's first arm with no bytes)
@@ -101,6 +107,8 @@ struct TcCtl {
     uint64_t xchg_full;   // partner: its results for this CTA's rows are in its slot
     uint64_t xchg_free;   // partner: it has read this CTA's slot
     uint64_t ids_ready;   // epilogue: the down unit's ids are emitted
+    uint64_t stg_full[kMaxStagingSlots];   // quantised: a staging slot's raw blocks have landed
+    uint64_t stg_empty[kMaxStagingSlots];  // quantised: a staging slot has been expanded
     uint32_t tmem_base;
     int last;             // this CTA finished last: it resets the launch's counters
     volatile int abort;
@@ -334,15 +342,16 @@ __device__ __forceinline__ void emit_ids16(const uint32_t *bits, const int *pref
 // ---------------------------------------------------------------------------------
 // Quantised weights (ggml Q8_0 / Q4_0 blocks of 32 along d, in the "split" row
 // layout: the row's quant bytes, then its fp16 scales).  The MMA still reads
-// fp16 operands, so the producers expand the gathered blocks in shared memory:
-// every producer thread owns whole blocks (one 32-element block of one row =
-// a task), copies their raw bytes and their scale pair with cp.async into its
-// own part of a staging slot, and once its copies of that stage have landed
-// (cp.async.wait_group: the thread's own groups, no barrier) writes the 32
-// fp16 values into the stage's swizzled operand tile and arrives on the
-// stage's `full` barrier.  Several stages are staged ahead of the operand
-// ring, so the quant bytes in flight do not depend on the (four times larger)
-// fp16 tiles.  Values: q * scale computed in fp32 and rounded to fp16 once --
+// fp16 operands, so the producers expand the gathered blocks in shared memory.
+// The producer warps split in two.  Copying threads issue, per stage, the raw
+// bytes and scale pair of every task (one 32-element block of one row) with
+// cp.async into a staging slot and arrive on the slot's barrier when their
+// copies land (cp.async.mbarrier.arrive); they run up to nstg stages ahead.
+// Expanding threads wait for a slot, write the 32 fp16 values of each task
+// into the stage's swizzled operand tile, arrive on the stage's `full`
+// barrier and free the slot.  Copy latency thus overlaps the expansion of
+// earlier stages, and the quant bytes in flight do not depend on the (four
+// times larger) fp16 tiles.  Values: q * scale computed in fp32 and rounded to fp16 once --
 // the product of an 8-bit integer and an fp16 scale is exact in fp32, so this
 // is the oracle's dequantised value (spbo_dequantize) rounded to the operand
 // type.
@@ -408,12 +417,12 @@ struct QuantProducer {
         }
     }
 
-    __device__ __forceinline__ void issue(const TcArgs &a, const QStage &q, int slot) const {
+    __device__ __forceinline__ void issue(const TcArgs &a, const QStage &q, int slot, int lt, int nthr) const {
         const uint32_t sq = smem_u32(stg + (size_t)slot * a.stg_bytes);
         const uint32_t ss = sq + (uint32_t)a.stg_tasks * (a.wtype == SPB_W_Q8_0 ? 32u : 16u);
         const int nt = (a.inject & 16) ? 0 : tasks_of(a, q);
         const int sco = a.wtype == SPB_W_Q8_0 ? a.d : a.d / 2;  // scales after the quant bytes
-        for (int i = pt; i < nt; i += kProducerThreads) {
+        for (int i = lt; i < nt; i += nthr) {
             const uint8_t *row;
             int gb, r, blk;
             task_src(a, q, i, row, gb, r, blk);
@@ -425,20 +434,21 @@ struct QuantProducer {
             }
             cp_async4(ss + i * 4, row + sco + (gb & ~1) * 2);
         }
-        cp_async_commit();
+        // the slot's barrier completes once every copying thread's copies landed
+        cp_async_mbar_arrive(&ctl->stg_full[slot]);
     }
 
     // The oldest staged stage has landed (this thread's part): expand it into
     // its ring unit once the MMAs have released the unit.
-    __device__ __forceinline__ bool finish(const TcArgs &a, const QStage &q, int slot) const {
-        if (pt == 0) stage_stamp(a, q.t, 3);
+    __device__ __forceinline__ bool finish(const TcArgs &a, const QStage &q, int slot, int lt, int nthr) const {
+        if (lt == 0) stage_stamp(a, q.t, 3);
         if (!ring_wait_empty(q.t, NU, ctl, a)) return false;
-        if (pt == 0) stage_stamp(a, q.t, 0);
+        if (lt == 0) stage_stamp(a, q.t, 0);
         const uint8_t *sq = stg + (size_t)slot * a.stg_bytes;
         const uint8_t *ss = sq + (size_t)a.stg_tasks * (a.wtype == SPB_W_Q8_0 ? 32 : 16);
         const uint32_t ubase = smem_u32(ring + (size_t)(q.t % NU) * a.unit_bytes);
         const int nt = (a.inject & 8) ? 0 : tasks_of(a, q);
-        for (int i = pt; i < nt; i += kProducerThreads) {
+        for (int i = lt; i < nt; i += nthr) {
             int r, blk, gb;
             task_of(a, q, i, r, blk, gb);
             // the block's scale in both halves of a half2
@@ -499,7 +509,7 @@ struct QuantProducer {
         if (q.kind == 1) {
             // positions past the chunk, up to the next multiple of 16: zero rows
             const int nr16 = (q.rows + 15) & ~15;
-            for (int i = q.rows * 32 + pt; i < nr16 * 32; i += kProducerThreads) {
+            for (int i = q.rows * 32 + lt; i < nr16 * 32; i += nthr) {
                 const int r = i >> 5, c = i & 31, mb = c >> 3, c8 = c & 7, kr = r & 7;
                 st_shared_v4(ubase + mb * kDnLbo + (r >> 3) * 1024 + kr * 128 + ((c8 ^ kr) << 4),
                              make_uint4(0u, 0u, 0u, 0u));
@@ -508,30 +518,11 @@ struct QuantProducer {
         // (the MMA issuer fences its view of these generic-proxy writes
         // against the async proxy once the stage's barrier completes)
         mbar_arrive(&ctl->full[q.t % NU]);
-        if (pt == 0) stage_stamp(a, q.t, 1);
+        mbar_arrive(&ctl->stg_empty[slot]);  // the copying threads may refill the slot
+        if (lt == 0) stage_stamp(a, q.t, 1);
         return true;
     }
 
-    // Stage t's copies are issued into staging slot t % nstg; stage
-    // t - nstg, whose slot that was, is expanded first (its copies are this
-    // thread's oldest outstanding group).
-    __device__ __forceinline__ bool step(const TcArgs &a, int t) const {
-        if (t >= a.nstg) {
-            cp_async_wait(a.nstg - 1);
-            if (!finish(a, stage(t - a.nstg), (t - a.nstg) % a.nstg)) return false;
-        }
-        issue(a, stage(t), t % a.nstg);
-        return true;
-    }
-
-    // Expands the stages still staged after stage `end` - 1 was issued.
-    __device__ __forceinline__ bool drain(const TcArgs &a, int end) const {
-        for (int t = max(0, end - a.nstg); t < end; ++t) {
-            cp_async_wait(min(end - 1 - t, kMaxStaging));
-            if (!finish(a, stage(t), t % a.nstg)) return false;
-        }
-        return true;
-    }
 };
 
 // kQuant: the producers expand quantised rows (a separate instantiation, so
@@ -572,7 +563,7 @@ ffn_tc_kernel(const __grid_constant__ TcMaps maps, const TcArgs a) {
 
     if (tid == 0) {
         for (int i = 0; i < NU; ++i) {
-            mbar_init(&ctl->full[i], kProducerThreads);
+            mbar_init(&ctl->full[i], kQuant ? kQExpThreads : kProducerThreads);
             mbar_init(&ctl->tma[i], 1);
             mbar_init(&ctl->empty[i], 1);
         }
@@ -583,6 +574,11 @@ ffn_tc_kernel(const __grid_constant__ TcMaps maps, const TcArgs a) {
         mbar_init(&ctl->xchg_full, kEpiWarps * 32);
         mbar_init(&ctl->xchg_free, kEpiWarps * 32);
         mbar_init(&ctl->ids_ready, kEpiWarps * 32);
+        if (kQuant)
+            for (int i = 0; i < a.nstg; ++i) {
+                mbar_init(&ctl->stg_full[i], kQCopyThreads);
+                mbar_init(&ctl->stg_empty[i], kQExpThreads);
+            }
         ctl->abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -719,16 +715,28 @@ ffn_tc_kernel(const __grid_constant__ TcMaps maps, const TcArgs a) {
         const QuantProducer qp{ctl, ring, stg, pt, NU, nkb, rank ? a.wu : a.wg, (KG ? clu % KG : 0), KG, m, n, ntile,
                                gu_ids, dn_ids, Q0, Q1};
         bool ok = !ctl->abort;
-        const int ngu = ntile * KG, total = ngu + ndn;
-        int t = 0;
-        for (; t < total && ok; ++t) {
-            // the down stages' ids come from the epilogue warps
-            if (t == ngu) ok = wait_bar(&ctl->ids_ready, 0, ctl, a, kErrTimeoutAcc, a.hint);
-            if (ok) ok = qp.step(a, t);
+        const int ngu = ntile * KG, total = ngu + ndn, S = a.nstg;
+        if (pt < kQCopyThreads) {
+            // copying threads: stage t's raw blocks into slot t % S once the
+            // expansion of stage t - S has emptied it; they run up to S
+            // stages ahead of the expansion
+            for (int t = 0; t < total && ok; ++t) {
+                // the down stages' ids come from the epilogue warps
+                if (t == ngu) ok = wait_bar(&ctl->ids_ready, 0, ctl, a, kErrTimeoutAcc, a.hint);
+                if (ok && t >= S)
+                    ok = wait_bar(&ctl->stg_empty[t % S], (uint32_t)(t / S - 1) & 1u, ctl, a, kErrTimeoutFull, a.hint);
+                if (ok) qp.issue(a, qp.stage(t), t % S, pt, kQCopyThreads);
+            }
+            // Every copy this thread issued lands before the CTA can exit.
+            cp_async_wait_all();
+        } else {
+            // expanding threads: each landed slot into its ring unit
+            const int lt = pt - kQCopyThreads;
+            for (int t = 0; t < total && ok; ++t) {
+                ok = wait_bar(&ctl->stg_full[t % S], (uint32_t)(t / S) & 1u, ctl, a, kErrTimeoutFull, a.hint);
+                if (ok) ok = qp.finish(a, qp.stage(t), t % S, lt, kQExpThreads);
+            }
         }
-        if (ok) qp.drain(a, total);
-        // Every copy this thread issued lands before the CTA can exit.
-        cp_async_wait_all();
     } else if (warp >= kProducerWarp0 && warp < kMmaWarp && !dense) {
         // ------------------------------------------------------------ producers
         // (idle when whole row ranges stream: the TMA warp moves the rows)
