@@ -20,14 +20,16 @@ K steps replayed from CUDA graphs, barrier + synchronize on both sides, max
 over ranks; the K-step region is repeated and the median reported.
 
 Under torchrun (WORLD_SIZE > 1) the layer's neurons are sharded across the
-ranks (gate/up rows, W_down rows; one NCCL all-reduce of the [B][d] fp32
-partial outputs per layer): strong scaling of the same layer, so N = 1 is
+ranks (gate/up rows, W_down rows; one all-reduce of the [B][d] fp32
+partial outputs per layer: NCCL's, or with --peer the library's one-shot
+kernel over NVLink peer memory): strong scaling of the same layer, so N = 1 is
 the single-GPU run.  --replicas runs independent copies instead.
 
 The JSON line adds: per_batch (the same layer at B = 1..32), dense_cublas
 (the dense FFN through cuBLAS fp16 GEMMs with fp32 accumulation, same
 config), device_error (the workspace's error word after every timed region;
-non-zero fails the run), shard_parity / allreduce_us when sharded.
+non-zero fails the run), shard_parity / allreduce_us (the step's collective
+alone) / nccl_allreduce_us when sharded.
 
 --impl reference times the reference's CPU path (a PyTorch masked-dense FFN
 on all host cores; the reference itself has no CPU FFN and its GPU code is
@@ -75,6 +77,8 @@ def parse():
     ap.add_argument("--repeats", type=int, default=0, help="timed K-step regions (0 = enough for ~0.3 s)")
     ap.add_argument("--shard", action="store_true", help="shard the layer's neurons across the ranks")
     ap.add_argument("--replicas", action="store_true", help="under torchrun: independent replicas, no sharding")
+    ap.add_argument("--peer", action="store_true",
+                    help="sharded: the library's one-shot peer-memory all-reduce instead of NCCL's")
     ap.add_argument("--wtype", choices=["f16", "q8_0", "q4_0"], default="f16",
                     help="weight format (config 4: ggml block quantisation of fp32 N(0, 0.02^2) weights)")
     ap.add_argument("--predictor", action="store_true",
@@ -325,6 +329,10 @@ def run_ours(a):
              for _ in range(L)]
     stream = torch.cuda.Stream(device)
     peak, peak_kind = hbm_peak()
+    peer = None
+    if sharded and a.peer:  # the exchange step through the library's all-reduce over NVLink peer memory
+        from spbatch_b200.shard import PeerAllReduce
+        peer = PeerAllReduce(max(SWEEP_BATCHES + (a.batch,)) * d, device)
     errors = []
 
     def measure(B, headline):
@@ -347,14 +355,19 @@ def run_ours(a):
             xx = ly["x"] if x is None else x
             ll = ly["lab"] if lab is None else lab
             o = ly["out"] if out is None else out
+            # sharded with the peer all-reduce: the layer writes its partial
+            # into the rank's mapped buffer, the reduction writes `o`
+            po = peer.partial(B * d).view(B, d) if peer is not None else o
             if a.predictor:
                 spb.predict(P[i][0], P[i][1], xx, k=k, bits_out=ly["bits"], labels=False, workspace=pw)
-                spb.ffn_forward(*Wl[i], xx, bits=ly["bits"], f=f1 - f0, wtype=wtype, out=o,
+                spb.ffn_forward(*Wl[i], xx, bits=ly["bits"], f=f1 - f0, wtype=wtype, out=po,
                                 per_token_mask=bool(a.per_token), path=path, workspace=ws)
             else:
-                spb.ffn_forward(*Wl[i], xx, ll, wtype=wtype, out=o, per_token_mask=bool(a.per_token), path=path,
+                spb.ffn_forward(*Wl[i], xx, ll, wtype=wtype, out=po, per_token_mask=bool(a.per_token), path=path,
                                 workspace=ws)
-            if sharded:  # one all-reduce of the [B][d] partial outputs (NCCL)
+            if peer is not None:  # one all-reduce of the [B][d] partial outputs
+                peer.reduce(B * d, o)
+            elif sharded:
                 dist.all_reduce(o)
 
         timer = Timer(torch, stream, L, fwd, graphs=True)
@@ -414,13 +427,23 @@ def run_ours(a):
             del Wfull, parts
         dist.broadcast(ok, 0)
         shard_parity = bool(ok.item())
+    nccl_us = None
     if sharded:
         # the collective alone: 50 all-reduces of the [B][d] fp32 output
-        # captured in one graph, replayed on the compute stream
+        # captured in one graph, replayed on the compute stream -- the one the
+        # step uses, and NCCL's for comparison
         buf = torch.zeros((a.batch, d), device=device)
         art = Timer(torch, stream, 1, lambda i: dist.all_reduce(buf), graphs=True)
         art.warm(3)
-        allreduce_us = art.time(50, 5, dist, device)[0] * 1e3
+        nccl_us = art.time(50, 5, dist, device)[0] * 1e3
+        allreduce_us = nccl_us
+        if peer is not None:
+            n = a.batch * d
+            prt = Timer(torch, stream, 1, lambda i: peer.reduce(n, buf), graphs=True)
+            prt.warm(3)
+            allreduce_us = prt.time(50, 5, dist, device)[0] * 1e3
+            if peer.error():
+                errors.append(100 + peer.error())
 
     # e2e: pinned host inputs copied in and the output copied back every step
     pinned = [dict(x=torch.from_numpy(ly["x_np"]).pin_memory(), lab=torch.from_numpy(ly["lab_np"]).pin_memory(),
@@ -462,6 +485,9 @@ def run_ours(a):
     if sharded:
         rec["shard_parity"] = shard_parity
         rec["allreduce_us"] = allreduce_us
+        rec["nccl_allreduce_us"] = nccl_us
+        rec["collective"] = ("one-shot all-reduce over NVLink peer memory (spb_allreduce_peer, own kernel)"
+                             if peer is not None else "NCCL all-reduce")
         rec["parallelism"] = f"neuron-sharded tp{ws_n}"
 
     if sweep:
@@ -515,7 +541,7 @@ def config_dict(a, d, f, f_shard, k, Us, Us_full, L, bytes_step, ws_n, sharded):
                           if a.predictor else None),
             "l2": f"inputs larger than L2: {L} layer copies rotated, "
                   f"{L * bytes_step / 1e6:.0f} MB touched per cycle vs 126 MB L2",
-            "parallelism": (f"neuron-sharded tp{ws_n} + NCCL all-reduce" if sharded else
+            "parallelism": (f"neuron-sharded tp{ws_n} + one all-reduce" if sharded else
                             f"replicas x{ws_n}" if ws_n > 1 else "single GPU")}
 
 

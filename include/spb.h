@@ -198,6 +198,36 @@ int spb_union_static(const float *idx, int B, int f, int group, int32_t *merge_i
                      uint32_t *tok_bits, void *stream);
 
 /*
+ * Neuron sharding's exchange step without a library collective: a one-shot
+ * all-reduce of the ranks' [B][d] fp32 partial outputs over NVLink peer
+ * memory.  Replaces the NCCL all-reduce the sharded layer would otherwise
+ * issue after the down projection (the reference is single-GPU: ffn_test.cu
+ * pins one device; its down projection ends at cuda/kernel.cu:706-816).
+ *
+ * Set-up, once: each rank allocates one device region holding its sync words
+ * (spb_peer_sync_bytes(), zero-filled once) and its receive slots
+ * [2][world][stride] fp32, exports the region's pointer with spb_peer_export
+ * into spb_peer_handle_bytes() bytes, the ranks exchange the handles on the
+ * host, and each rank maps its peers' regions with spb_peer_import (CUDA IPC;
+ * undo with spb_peer_close).
+ *
+ * spb_allreduce_peer: partial = this rank's n floats (local); recv[r] /
+ * syncs[r] = rank r's receive slots / sync words as this rank's GPU addresses
+ * them (its own at r == rank); out receives the rank-ordered sum, bit-identical
+ * on every rank.  n and stride are multiples of 4 with n <= stride; pointers
+ * 16-byte aligned.  One launch, stream ordered after the kernel that wrote
+ * `partial`.  Every rank makes the same sequence of calls.  Bounded waits:
+ * *err (device word) receives 1 if a peer never arrived.
+ */
+size_t spb_peer_handle_bytes(void);
+size_t spb_peer_sync_bytes(void);
+int spb_peer_export(const void *dev_ptr, void *handle_out);
+int spb_peer_import(const void *handle, void **dev_ptr_out);
+int spb_peer_close(void *dev_ptr);
+int spb_allreduce_peer(const float *partial, float *const *recv, uint32_t *const *syncs, int world, int rank,
+                       int64_t stride, float *out, int64_t n, uint32_t *err, void *stream);
+
+/*
  * Tracing: while enabled, tensor-path launches write per-CTA phase stamps
  * (%globaltimer ns, 16 u64 slots per CTA: start, union scanned, gate/up
  * issued, gate/up MMAs done, gate/up accumulators ready, h published, first

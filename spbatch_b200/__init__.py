@@ -81,6 +81,12 @@ def _bind(L: C.CDLL) -> None:
     L.spb_ffn_forward.argtypes = [P, P, P, I, P, P, I, I, I, I, I, I, P, P, P, P, Z, P]
     L.spb_ffn_launches.argtypes = [I, I, I, I]
     L.spb_trace_enable.argtypes = [P, Z]
+    L.spb_peer_handle_bytes.restype = Z
+    L.spb_peer_sync_bytes.restype = Z
+    L.spb_peer_export.argtypes = [P, P]
+    L.spb_peer_import.argtypes = [P, C.POINTER(C.c_void_p)]
+    L.spb_peer_close.argtypes = [P]
+    L.spb_allreduce_peer.argtypes = [P, P, P, I, I, C.c_int64, P, C.c_int64, P, P]
 
 
 def _check(rc: int, what: str) -> None:
