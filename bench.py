@@ -111,11 +111,11 @@ def hbm_peak():
 
 
 def pred_launches(B):
-    """Kernels of this library that the predictor adds to a step (top-k set
-    words): none at B = 1 (spb_predict_ffn runs it inside the layer's
-    launch); hidden, logit and two selects up to 16 tokens; above, x -> fp16,
-    a histogram pass and two selects around two cuBLASLt GEMMs."""
-    return 0 if B == 1 else 4
+    """Kernels of this library that spb_predict launches for set words (top-k,
+    no index list): one fused launch at B = 1; hidden, logit and two selects
+    up to 16 tokens; above, x -> fp16, a histogram pass and two selects around
+    two cuBLASLt GEMMs."""
+    return 1 if B == 1 else 4
 
 
 def workload_name(a, U, B=None):
@@ -358,9 +358,10 @@ def run_ours(a):
             # sharded with the peer all-reduce: the layer writes its partial
             # into the rank's mapped buffer, the reduction writes `o`
             po = peer.partial(B * d).view(B, d) if peer is not None else o
-            if a.predictor:  # predictor + layer (one launch at B = 1, fp16), set words in between otherwise
-                spb.predict_ffn(P[i][0], P[i][1], *Wl[i], xx, k, wtype=wtype, out=po, bits_out=ly["bits"],
-                                per_token_mask=bool(a.per_token), workspace=ws, pred_workspace=pw)
+            if a.predictor:
+                spb.predict(P[i][0], P[i][1], xx, k=k, bits_out=ly["bits"], labels=False, workspace=pw)
+                spb.ffn_forward(*Wl[i], xx, bits=ly["bits"], f=f1 - f0, wtype=wtype, out=po,
+                                per_token_mask=bool(a.per_token), path=path, workspace=ws)
             else:
                 spb.ffn_forward(*Wl[i], xx, ll, wtype=wtype, out=po, per_token_mask=bool(a.per_token), path=path,
                                 workspace=ws)

@@ -180,27 +180,6 @@ int spb_predict(const void *p1, const void *p2, const float *x, int B, int d, in
                 void *workspace, size_t workspace_bytes, void *stream);
 
 /*
- * The DejaVu predictor and the sparse FFN layer it drives, in one call: the
- * top-k of x's logits (exactly spb_predict's sets, k > 0) is the active set
- * of spb_ffn_forward_bits on the same x (per-token mask, fp32 out [B][d]).
- * At B = 1 with fp16 weights this is ONE launch: the streaming kernel first
- * runs the predictor in its still-unused stage ring (P2 slices copied into
- * shared memory, two grid barriers, every CTA deriving the whole set from
- * the logits and the histogram) and then streams the set's rows -- no
- * [B][f] labels, no bit words through HBM between the two.  Other shapes run
- * spb_predict then spb_ffn_forward_bits.  bits_out ([B][ceil(f/32)]) receives
- * the predicted set if non-null.  workspace: spb_ffn_workspace_bytes(B, d, f,
- * 0), zero-filled once; pred_workspace: spb_predict_workspace_bytes(B, D, f).
- * Replaces the predictor -> get_idx_cuda -> MLP_BS chain of a DejaVu-driven
- * layer (DejaVu_predictor/main_mlp.py:137-141, trainer_mlp.py:35-37,
- * cuda/ffn_test.cu:129-142).
- */
-int spb_predict_ffn(const void *p1, const void *p2, int D, int k, const void *w_gate, const void *w_up,
-                    const void *w_down, int wtype, const float *x, int B, int d, int f, int act, int per_token_mask,
-                    float *out, uint32_t *bits_out, void *workspace, size_t workspace_bytes, void *pred_workspace,
-                    size_t pred_workspace_bytes, void *stream);
-
-/*
  * Allocation-free variant of spb_union for callers that cannot allocate
  * device memory (a framework allocator owns the device, a plug-in receives
  * only its input and output buffers, or a latency-critical path must not call

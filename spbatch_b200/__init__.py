@@ -81,7 +81,6 @@ def _bind(L: C.CDLL) -> None:
     L.spb_ffn_forward.argtypes = [P, P, P, I, P, P, I, I, I, I, I, I, P, P, P, P, Z, P]
     L.spb_ffn_launches.argtypes = [I, I, I, I]
     L.spb_trace_enable.argtypes = [P, Z]
-    L.spb_predict_ffn.argtypes = [P, P, I, I, P, P, P, I, P, I, I, I, I, I, P, P, P, Z, P, Z, P]
     L.spb_peer_handle_bytes.restype = Z
     L.spb_peer_sync_bytes.restype = Z
     L.spb_peer_export.argtypes = [P, P]
@@ -212,32 +211,6 @@ def quantize(w, wtype: int):
         raise SpbError("quantize: d must be a multiple of 32")
     out = np.zeros((rows, rb), np.uint8)
     _check(lib().spb_quantize(w.ctypes.data, rows, d, wtype, out.ctypes.data), "spb_quantize")
-    return out
-
-
-def predict_ffn(p1, p2, w_gate, w_up, w_down, x, k: int, *, wtype: int = W_F16, act: int = ACT_RELU_MUL,
-                per_token_mask: bool = True, out=None, bits_out=None, workspace=None, pred_workspace=None,
-                stream=None, check: bool = False):
-    """DejaVu predictor + sparse FFN layer on the same x (spb_predict_ffn):
-    the top-k of the predictor's logits is the layer's active set.  One
-    launch at B = 1 with fp16 weights.  Returns out [B][d] fp32; bits_out
-    ([B][ceil(f/32)] int32) receives the predicted set if given."""
-    import torch
-    _require_cuda(p1, p2, w_gate, w_up, w_down, x, out, bits_out, workspace, pred_workspace)
-    B, d = x.shape
-    D, f = p1.shape[0], p2.shape[0]
-    if out is None:
-        out = torch.empty((B, d), dtype=torch.float32, device=x.device)
-    ws = workspace if workspace is not None else new_workspace(B, d, f, 0, x.device)
-    pw = pred_workspace if pred_workspace is not None else predict_workspace(B, D, f, x.device)
-    _check(lib().spb_predict_ffn(p1.data_ptr(), p2.data_ptr(), D, k, w_gate.data_ptr(), w_up.data_ptr(),
-                                 w_down.data_ptr(), wtype, x.data_ptr(), B, d, f, act, int(per_token_mask),
-                                 out.data_ptr(), _ptr(bits_out), ws.data_ptr(), ws.numel(), pw.data_ptr(), pw.numel(),
-                                 _stream(stream)), "spb_predict_ffn")
-    if check:
-        code = device_error(ws)
-        if code:
-            raise SpbError(f"predict_ffn: device error {code}")
     return out
 
 

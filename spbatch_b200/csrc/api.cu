@@ -362,70 +362,6 @@ int spb_predict(const void *p1, const void *p2, const float *x, int B, int d, in
                           static_cast<cudaStream_t>(stream));
 }
 
-int spb_predict_ffn(const void *p1, const void *p2, int D, int k, const void *w_gate, const void *w_up,
-                    const void *w_down, int wtype, const float *x, int B, int d, int f, int act, int per_token_mask,
-                    float *out, uint32_t *bits_out, void *workspace, size_t workspace_bytes, void *pred_workspace,
-                    size_t pred_workspace_bytes, void *stream) {
-    if (!p1 || !p2 || !w_gate || !w_up || !w_down || !x || !out)
-        return fail(SPB_ERR_INVALID, "spb_predict_ffn: null pointer");
-    if (B <= 0 || d <= 0 || D <= 0 || f <= 0 || k <= 0 || k >= f)
-        return fail(SPB_ERR_INVALID, "spb_predict_ffn: bad shape (0 < k < f)");
-    if (d % 256 || D % 256) return fail(SPB_ERR_INVALID, "spb_predict_ffn: d and D must be multiples of 256");
-    if (!aligned16(p1) || !aligned16(p2) || !aligned16(w_gate) || !aligned16(w_up) || !aligned16(w_down) ||
-        !aligned16(x) || !aligned16(out))
-        return fail(SPB_ERR_INVALID, "spb_predict_ffn: weights, x and out must be 16-byte aligned");
-    if (act != SPB_ACT_RELU_MUL && act != SPB_ACT_RELU_RELU_MUL)
-        return fail(SPB_ERR_INVALID, "spb_predict_ffn: unknown activation");
-    if (words_of(f) > 1024) return fail(SPB_ERR_UNSUPPORTED, "spb_predict_ffn: f > 32768");
-    Workspace ws = carve_workspace(workspace, B, d, f, 0);
-    if (!workspace || workspace_bytes < ws.bytes) return fail(SPB_ERR_WORKSPACE, "spb_predict_ffn: workspace too small");
-    const size_t pneed = spb_predict_workspace_bytes_d(B, d, D, f);
-    if (!pred_workspace || pred_workspace_bytes < pneed)
-        return fail(SPB_ERR_WORKSPACE, "spb_predict_ffn: predictor workspace too small");
-    __half *hidden = nullptr;
-    float *logits = nullptr;
-    PredScratch sc{};
-    predict_layout(B, d, D, f, static_cast<char *>(pred_workspace), &hidden, &logits, &sc);
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
-    if (B == 1 && wtype == SPB_W_F16 && stream_ffn_supported(wtype, B, d)) {
-        StreamFfnArgs sa{};
-        sa.wg = w_gate;
-        sa.wu = w_up;
-        sa.wd = w_down;
-        sa.wtype = wtype;
-        sa.x = x;
-        sa.B = B;
-        sa.d = d;
-        sa.f = f;
-        sa.act = act;
-        sa.per_token = per_token_mask;
-        sa.out = out;
-        sa.err = ws.err;
-        sa.seg_bits = ws.seg_bits;
-        sa.tok_bits = ws.tok_bits;
-        sa.grid_bar = ws.grid_bar;
-        sa.launch_ctr = ws.launch_ctr;
-        sa.zero_flag = ws.zero_flag;
-        sa.p1 = static_cast<const __half *>(p1);
-        sa.p2 = static_cast<const __half *>(p2);
-        sa.hidden = hidden;
-        sa.logits = logits;
-        sa.hist = sc.hist;
-        sa.bits_out = bits_out;
-        sa.D = D;
-        sa.k = k;
-        const int rc = launch_stream_ffn(sa, st);
-        if (rc != SPB_ERR_UNSUPPORTED) return rc;  // else: too large for one launch's shared memory
-    }
-    // the composition: the predictor's set words, then the layer
-    uint32_t *bits = bits_out ? bits_out : sc.bits;
-    if (int rc = launch_predict(static_cast<const __half *>(p1), static_cast<const __half *>(p2), x, B, d, D, f, k,
-                                0.0f, nullptr, bits, nullptr, nullptr, logits, hidden, sc, st))
-        return rc;
-    return ffn_impl(w_gate, w_up, w_down, wtype, x, nullptr, bits, nullptr, nullptr, B, d, f, act, per_token_mask,
-                    SPB_PATH_AUTO, out, nullptr, nullptr, workspace, workspace_bytes, stream);
-}
-
 int spb_trace_enable(void *device_buffer, size_t slots) {
     std::lock_guard<std::mutex> lk(g_trace_mu);
     g_trace_buf = device_buffer;

@@ -65,14 +65,6 @@ struct StreamFfnArgs {
     unsigned long long *grid_bar;    // workspace: grid-barrier arrival counter
     unsigned long long *launch_ctr;  // workspace: monotonic CTA ticket counter
     unsigned long long *zero_flag;   // workspace: launch number + 1 once `out` is zeroed
-    // predictor-fused mode (B = 1, fp16): the DejaVu predictor's top-k set
-    // is the active set; null p1 otherwise
-    const __half *p1 = nullptr, *p2 = nullptr;  // [D][d], [f][D]
-    __half *hidden = nullptr;                    // [D] scratch
-    float *logits = nullptr;                     // [f] scratch
-    uint32_t *hist = nullptr;                    // [2048] scratch
-    uint32_t *bits_out = nullptr;                // [W] the predicted set, or null
-    int D = 0, k = 0;
 };
 bool stream_ffn_supported(int wtype, int B, int d);
 // drop-in up projection on the bulk-copy streaming design (fp16, d <= 4096)

@@ -44,7 +44,6 @@
 // an error code in the workspace and finishes without waiting again.  After
 // such an error the workspace must be zeroed before it is used again.
 #include "spb_internal.h"
-#include "spb_pred.cuh"
 #include "spb_quant.cuh"
 #include "spb_scan.cuh"
 #include "tc_ptx.cuh"
@@ -92,14 +91,6 @@ struct SfArgs {
     int rb;           // row bytes (multiple of 16)
     int stage_bytes;  // 3 * rb
     int off_bits, off_nid, off_mask, off_red, off_stage;
-    // predictor-fused mode (one token): the DejaVu predictor runs first and
-    // its top-k set is the union
-    const __half *p1, *p2;  // [D][d], [f][D] fp16
-    __half *hidden;         // [D] scratch
-    float *logits;          // [f] scratch (written, then read by every CTA)
-    uint32_t *hist;         // [kHistBins] scratch
-    uint32_t *bits_out;     // [W] the predicted set, or null
-    int D, k, prows, off_pred;  // P2 rows per CTA; shared-memory offset of the predictor's region
 };
 
 // Stamps written when tracing is enabled (spb_trace_enable): 0 start,
@@ -231,7 +222,7 @@ __device__ __forceinline__ float sf_act(float g, float u, int act) {
 
 // NT: tokens (B <= NT), CPT: 8-element chunks per consumer thread
 // (ceil(d / 4096)).
-template <int NT, int WT, int CPT, bool kPred = false>
+template <int NT, int WT, int CPT>
 __global__ void __launch_bounds__(kSfThreads, 1) stream_ffn_kernel(const SfArgs a) {
     extern __shared__ __align__(1024) uint8_t smem[];
     SfCtl *ctl = reinterpret_cast<SfCtl *>(smem);
@@ -297,289 +288,101 @@ __global__ void __launch_bounds__(kSfThreads, 1) stream_ffn_kernel(const SfArgs 
     // ---- the batch union: union words [W] and token words [NT][W] ----
     uint32_t *ubits = reinterpret_cast<uint32_t *>(smem + a.off_bits);
     uint32_t *tbits = ubits + a.W;
-    if constexpr (kPred) {
-        // ---- the DejaVu predictor's top-k set as the union (one token) ----
-        // The stage ring is free until the rows stream: it holds x (fp16),
-        // hidden, this CTA's P2 slice and, once the logits exist, all
-        // logits and the threshold bin's candidates.  Same arithmetic and
-        // selection as spb_predict (bit-exact against the oracle).
-        uint8_t *pb = smem + a.off_pred;
-        __half *xs = reinterpret_cast<__half *>(pb);
-        __half *hs = xs + a.d;
-        const int rpad = (a.prows + 3) & ~3;
-        uint32_t *keys = reinterpret_cast<uint32_t *>(hs + a.D);
-        uint32_t *shist = keys + rpad;
-        __half *p2s = reinterpret_cast<__half *>(shist + kHistBins);
-        uint2 *cand = reinterpret_cast<uint2 *>(p2s);
-        float *lgs = reinterpret_cast<float *>(cand + a.f);
-        __shared__ int s_nc, s_need, pw_tot[kSfWarps + 2];
-        __shared__ uint32_t s_bin;
-        const int G = gridDim.x, D = a.D, f = a.f;
-        const int j0 = min(f, (int)blockIdx.x * a.prows), nrow = min(f, j0 + a.prows) - j0;
-        constexpr int kHidW = 8, kHidT = kHidW * 32;
-        if (warp >= kHidW) {
-            // P2 slice -> shared memory (16-byte cp.async)
-            const uint32_t dst = smem_u32(p2s);
-            const char *src = reinterpret_cast<const char *>(a.p2 + (size_t)j0 * D);
-            const int n16 = nrow * D / 8;
-            for (int i = tid - kHidT; i < n16; i += kSfThreads - kHidT) cp_async16_full(dst + i * 16, src + (size_t)i * 16);
-            cp_async_commit();
-            cp_async_wait_all();
-        } else {
-            for (int i = tid; i < a.d / 4; i += kHidT) {
-                const float4 v = __ldg(reinterpret_cast<const float4 *>(a.x) + i);
-                const __half2 h0 = __floats2half2_rn(v.x, v.y), h1 = __floats2half2_rn(v.z, v.w);
-                uint2 pk;
-                pk.x = *reinterpret_cast<const uint32_t *>(&h0);
-                pk.y = *reinterpret_cast<const uint32_t *>(&h1);
-                reinterpret_cast<uint2 *>(xs)[i] = pk;
-            }
-            for (int i = blockIdx.x * kHidT + tid; i < kHistBins; i += G * kHidT) a.hist[i] = 0u;
-            asm volatile("bar.sync 2, %0;" ::"r"(kHidT) : "memory");
-            const int hr = (D + G - 1) / G;
-            for (int r = blockIdx.x * hr + warp; r < min(D, (int)(blockIdx.x + 1) * hr); r += kHidW) {
-                float acc[1];
-                fixed_dot<1, 16>(a.p1 + (int64_t)r * a.d, xs, a.d, 1, acc);
-                if (lane == 0) a.hidden[r] = __float2half_rn(fmaxf(acc[0], 0.0f));
-            }
-        }
-        __syncthreads();
-        if (tid == 0) grid_wait(a.grid_bar, grid_arrive(a.grid_bar), ctl, a.err);
-        __syncthreads();
-        for (int i = tid; i < D / 8; i += kSfThreads)
-            reinterpret_cast<uint4 *>(hs)[i] = __ldcg(reinterpret_cast<const uint4 *>(a.hidden) + i);
-        for (int i = tid; i < kHistBins; i += kSfThreads) shist[i] = 0u;
-        __syncthreads();
-        {
-            constexpr int R = 4;
-            const int nfull = nrow / R * R;
-            for (int r = warp * R; r < nfull; r += kSfWarps * R + R) {
-                float acc[R];
-                fixed_dot_smem_rows<R>(p2s + (size_t)r * D, hs, D, acc);
-                if (lane < R) {
-                    float v = acc[0];
-#pragma unroll
-                    for (int q = 1; q < R; ++q)
-                        if (lane == q) v = acc[q];
-                    a.logits[j0 + r + lane] = v;
-                    keys[r + lane] = order_key(v);
-                }
-            }
-            for (int r = nfull + warp; r < nrow; r += kSfWarps + 1) {
-                float acc[1];
-                fixed_dot_smem_rows<1>(p2s + (size_t)r * D, hs, D, acc);
-                if (lane == 0) {
-                    a.logits[j0 + r] = acc[0];
-                    keys[r] = order_key(acc[0]);
-                }
-            }
-        }
-        __syncthreads();
-        for (int r = tid; r < nrow; r += kSfThreads) atomicAdd(&shist[keys[r] >> 21], 1u);
-        __syncthreads();
-        for (int i = tid; i < kHistBins; i += kSfThreads)
-            if (shist[i]) atomicAdd(a.hist + i, shist[i]);
-        __syncthreads();
-        if (tid == 0) grid_wait(a.grid_bar, grid_arrive(a.grid_bar), ctl, a.err);
-        __syncthreads();
-        // Every CTA: the histogram and all logits in one round trip, the
-        // threshold bin (thread i < 512 holds bins 2047 - 4i .. 2044 - 4i),
-        // the bin's candidates in id order, then the whole set.
-        uint32_t c4[4] = {0u, 0u, 0u, 0u}, sum = 0;
-        {
-            constexpr int U = 6;
-            const bool vec = (f & 3) == 0;
-            const int n4 = vec ? f >> 2 : 0;
-            float4 v[U];
-#pragma unroll
-            for (int u = 0; u < U; ++u) {
-                const int i = tid + u * kSfThreads;
-                v[u] = i < n4 ? __ldcg(reinterpret_cast<const float4 *>(a.logits) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
-            }
-            if (tid < kHistBins / 4)
-#pragma unroll
-                for (int q = 0; q < 4; ++q) c4[q] = __ldcg(a.hist + kHistBins - 1 - 4 * tid - q);
-#pragma unroll
-            for (int u = 0; u < U; ++u) {
-                const int i = tid + u * kSfThreads;
-                if (i < n4) reinterpret_cast<float4 *>(lgs)[i] = v[u];
-            }
-            for (int i = tid + U * kSfThreads; i < n4; i += kSfThreads)
-                reinterpret_cast<float4 *>(lgs)[i] = __ldcg(reinterpret_cast<const float4 *>(a.logits) + i);
-            if (!vec)
-                for (int j = tid; j < f; j += kSfThreads) lgs[j] = __ldcg(a.logits + j);
-        }
-#pragma unroll
-        for (int q = 0; q < 4; ++q) sum += c4[q];
-        constexpr int kW = kSfThreads / 32;
-        {
-            const int incl = warp_incl_scan((int)sum);
-            if (lane == 31) pw_tot[warp] = incl;
-            __syncthreads();
-            if (warp == 0) {
-                const int v = lane < kW ? pw_tot[lane] : 0;
-                const int vi = warp_incl_scan(v);
-                if (lane < kW) pw_tot[lane] = vi - v;
-            }
-            __syncthreads();
-            int before = pw_tot[warp] + incl - (int)sum;  // keys in bins above this thread's
-            const int k = a.k;
-            if (before < k && k <= before + (int)sum) {
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    if (before < k && k <= before + (int)c4[q]) {
-                        s_bin = kHistBins - 1 - 4 * tid - q;
-                        s_need = k - before;
-                    }
-                    before += c4[q];
-                }
-            }
-            __syncthreads();
-        }
-        const uint32_t bin = s_bin;
-        const int per = (f + kSfThreads - 1) / kSfThreads;
-        const int ja = min(f, tid * per), jb = min(f, ja + per);
-        {
-            int mine = 0;
-            for (int j = ja; j < jb; ++j) mine += (order_key(lgs[j]) >> 21) == bin;
-            const int mi = warp_incl_scan(mine);
-            if (lane == 31) pw_tot[warp] = mi;
-            __syncthreads();
-            if (warp == 0) {
-                const int v = lane < kW ? pw_tot[lane] : 0;
-                const int vi = warp_incl_scan(v);
-                if (lane < kW) pw_tot[lane] = vi - v;
-                if (lane == kW - 1) s_nc = vi;
-            }
-            __syncthreads();
-            int pos = pw_tot[warp] + mi - mine;
-            for (int j = ja; j < jb; ++j) {
-                const uint32_t key = order_key(lgs[j]);
-                if ((key >> 21) == bin) cand[pos++] = make_uint2(key, (uint32_t)j);
-            }
-            __syncthreads();
-        }
-        // the set's words: above the bin, or in it with rank < need (rank =
-        // candidates with a larger key, or an equal key and a lower id)
-        const int nc = s_nc, need = s_need;
+    if (a.tok_in) {
+        // Per-token bits from the caller: every CTA reads the B x W words
+        // (1.4 KB per token at f = 11008) through L2 -- no grid-wide step.
         for (int w = tid; w < a.W; w += kSfThreads) {
-            uint32_t word = 0;
-            for (int b = 0; b < 32; ++b) {
-                const int j = w * 32 + b;
-                if (j >= f) break;
-                const uint32_t key = order_key(lgs[j]);
-                bool on = (key >> 21) > bin;
-                if ((key >> 21) == bin) {
-                    int rank = 0;
-                    for (int q = 0; q < nc; ++q) {
-                        const uint2 o = cand[q];
-                        rank += o.x > key || (o.x == key && o.y < (uint32_t)j);
-                    }
-                    on = rank < need;
-                }
-                word |= (on ? 1u : 0u) << b;
-            }
-            ubits[w] = word;
-            tbits[w] = word;
-            if (a.bits_out && blockIdx.x == 0) a.bits_out[w] = word;
-        }
-    } else {
-        if (a.tok_in) {
-            // Per-token bits from the caller: every CTA reads the B x W words
-            // (1.4 KB per token at f = 11008) through L2 -- no grid-wide step.
-            for (int w = tid; w < a.W; w += kSfThreads) {
-                const uint32_t last = (w == a.W - 1 && (a.f & 31)) ? (1u << (a.f & 31)) - 1u : ~0u;
-                uint32_t un = 0;
+            const uint32_t last = (w == a.W - 1 && (a.f & 31)) ? (1u << (a.f & 31)) - 1u : ~0u;
+            uint32_t un = 0;
 #pragma unroll
-                for (int t = 0; t < NT; ++t) {
-                    const uint32_t bt = t < a.B ? (__ldg(a.tok_in + (int64_t)t * a.W + w) & last) : 0u;
-                    if (t < a.B) tbits[t * a.W + w] = bt;
-                    un |= bt;
-                }
-                ubits[w] = un;
+            for (int t = 0; t < NT; ++t) {
+                const uint32_t bt = t < a.B ? (__ldg(a.tok_in + (int64_t)t * a.W + w) & last) : 0u;
+                if (t < a.B) tbits[t * a.W + w] = bt;
+                un |= bt;
             }
-        } else if (a.local_union) {
-            // One token: every CTA reads the whole label row (f fp32, active if
-            // > 0) through L2 and builds the words itself -- no grid-wide step.
-            if ((a.f & 3) == 0 && (reinterpret_cast<uintptr_t>(a.idx) & 15u) == 0) {
-                // float4 loads: lane l of a warp covers neurons 4(q0 + l) .. +3; eight
-                // lanes' nibbles form one 32-neuron word.
-                constexpr int UR = NT == 1 ? 8 : (NT == 2 ? 4 : 2);  // rows of 544 float4 in flight
-                const int nq = a.f >> 2;
-                for (int base = 0; base < nq; base += UR * kSfThreads) {
-                    float4 v[UR][NT];
-        #pragma unroll
-                    for (int u = 0; u < UR; ++u) {
-                        const int q = base + u * kSfThreads + warp * 32 + lane;
-        #pragma unroll
-                        for (int t = 0; t < NT; ++t)
-                            v[u][t] = (q < nq && t < a.B) ? __ldg(reinterpret_cast<const float4 *>(a.idx + (int64_t)t * a.f) + q)
-                                                          : make_float4(0.f, 0.f, 0.f, 0.f);
-                    }
-        #pragma unroll
-                    for (int u = 0; u < UR; ++u) {
-                        const int q = base + u * kSfThreads + warp * 32 + lane;
-                        uint32_t un = 0;
-        #pragma unroll
-                        for (int t = 0; t < NT; ++t) {
-                            uint32_t nib = (v[u][t].x > 0.f ? 1u : 0u) | (v[u][t].y > 0.f ? 2u : 0u) |
-                                           (v[u][t].z > 0.f ? 4u : 0u) | (v[u][t].w > 0.f ? 8u : 0u);
-                            nib <<= 4 * (lane & 7);
-                            nib |= __shfl_xor_sync(0xffffffffu, nib, 1);
-                            nib |= __shfl_xor_sync(0xffffffffu, nib, 2);
-                            nib |= __shfl_xor_sync(0xffffffffu, nib, 4);
-                            un |= nib;
-                            if ((lane & 7) == 0 && q < nq && t < a.B) tbits[t * a.W + (q >> 3)] = nib;
-                        }
-                        if ((lane & 7) == 0 && q < nq) ubits[q >> 3] = un;
-                    }
+            ubits[w] = un;
+        }
+    } else if (a.local_union) {
+        // One token: every CTA reads the whole label row (f fp32, active if
+        // > 0) through L2 and builds the words itself -- no grid-wide step.
+        if ((a.f & 3) == 0 && (reinterpret_cast<uintptr_t>(a.idx) & 15u) == 0) {
+            // float4 loads: lane l of a warp covers neurons 4(q0 + l) .. +3; eight
+            // lanes' nibbles form one 32-neuron word.
+            constexpr int UR = NT == 1 ? 8 : (NT == 2 ? 4 : 2);  // rows of 544 float4 in flight
+            const int nq = a.f >> 2;
+            for (int base = 0; base < nq; base += UR * kSfThreads) {
+                float4 v[UR][NT];
+    #pragma unroll
+                for (int u = 0; u < UR; ++u) {
+                    const int q = base + u * kSfThreads + warp * 32 + lane;
+    #pragma unroll
+                    for (int t = 0; t < NT; ++t)
+                        v[u][t] = (q < nq && t < a.B) ? __ldg(reinterpret_cast<const float4 *>(a.idx + (int64_t)t * a.f) + q)
+                                                      : make_float4(0.f, 0.f, 0.f, 0.f);
                 }
-            } else {
-                for (int w = warp; w < a.W; w += kSfThreads / 32) {
-                    const int j = w * 32 + lane;
-                    float lab[NT];
-        #pragma unroll
-                    for (int t = 0; t < NT; ++t) lab[t] = (j < a.f && t < a.B) ? __ldg(a.idx + (int64_t)t * a.f + j) : 0.0f;
+    #pragma unroll
+                for (int u = 0; u < UR; ++u) {
+                    const int q = base + u * kSfThreads + warp * 32 + lane;
                     uint32_t un = 0;
-        #pragma unroll
+    #pragma unroll
                     for (int t = 0; t < NT; ++t) {
-                        const uint32_t bt = __ballot_sync(0xffffffffu, lab[t] > 0.0f);
-                        un |= bt;
-                        if (lane == 0 && t < a.B) tbits[t * a.W + w] = bt;
+                        uint32_t nib = (v[u][t].x > 0.f ? 1u : 0u) | (v[u][t].y > 0.f ? 2u : 0u) |
+                                       (v[u][t].z > 0.f ? 4u : 0u) | (v[u][t].w > 0.f ? 8u : 0u);
+                        nib <<= 4 * (lane & 7);
+                        nib |= __shfl_xor_sync(0xffffffffu, nib, 1);
+                        nib |= __shfl_xor_sync(0xffffffffu, nib, 2);
+                        nib |= __shfl_xor_sync(0xffffffffu, nib, 4);
+                        un |= nib;
+                        if ((lane & 7) == 0 && q < nq && t < a.B) tbits[t * a.W + (q >> 3)] = nib;
                     }
-                    if (lane == 0) ubits[w] = un;
+                    if ((lane & 7) == 0 && q < nq) ubits[q >> 3] = un;
                 }
             }
         } else {
-            // Several tokens: each CTA scans its share of the words and publishes
-            // them; after a grid barrier (the launch is cooperative) every CTA
-            // reads all words back.  Reading all B label rows in every CTA would
-            // cost B x f x 4 bytes of L2 traffic per SM.
-            const int w0 = (int)((int64_t)a.W * blockIdx.x / gridDim.x);
-            const int w1 = (int)((int64_t)a.W * (blockIdx.x + 1) / gridDim.x);
-            for (int w = w0 + warp; w < w1; w += kSfThreads / 32) {
+            for (int w = warp; w < a.W; w += kSfThreads / 32) {
                 const int j = w * 32 + lane;
                 float lab[NT];
-#pragma unroll
+    #pragma unroll
                 for (int t = 0; t < NT; ++t) lab[t] = (j < a.f && t < a.B) ? __ldg(a.idx + (int64_t)t * a.f + j) : 0.0f;
                 uint32_t un = 0;
-#pragma unroll
+    #pragma unroll
                 for (int t = 0; t < NT; ++t) {
                     const uint32_t bt = __ballot_sync(0xffffffffu, lab[t] > 0.0f);
                     un |= bt;
-                    if (lane == 0 && t < a.B) a.tok_bits[(int64_t)t * a.W + w] = bt;
+                    if (lane == 0 && t < a.B) tbits[t * a.W + w] = bt;
                 }
-                if (lane == 0) a.seg_bits[w] = un;
+                if (lane == 0) ubits[w] = un;
             }
-            __syncthreads();
-            if (tid == 0) grid_wait(a.grid_bar, grid_arrive(a.grid_bar), ctl, a.err);
-            __syncthreads();
-            for (int w = tid; w < a.W; w += kSfThreads) {
-                ubits[w] = __ldcg(a.seg_bits + w);
+        }
+    } else {
+        // Several tokens: each CTA scans its share of the words and publishes
+        // them; after a grid barrier (the launch is cooperative) every CTA
+        // reads all words back.  Reading all B label rows in every CTA would
+        // cost B x f x 4 bytes of L2 traffic per SM.
+        const int w0 = (int)((int64_t)a.W * blockIdx.x / gridDim.x);
+        const int w1 = (int)((int64_t)a.W * (blockIdx.x + 1) / gridDim.x);
+        for (int w = w0 + warp; w < w1; w += kSfThreads / 32) {
+            const int j = w * 32 + lane;
+            float lab[NT];
 #pragma unroll
-                for (int t = 0; t < NT; ++t)
-                    if (t < a.B) tbits[t * a.W + w] = __ldcg(a.tok_bits + (int64_t)t * a.W + w);
+            for (int t = 0; t < NT; ++t) lab[t] = (j < a.f && t < a.B) ? __ldg(a.idx + (int64_t)t * a.f + j) : 0.0f;
+            uint32_t un = 0;
+#pragma unroll
+            for (int t = 0; t < NT; ++t) {
+                const uint32_t bt = __ballot_sync(0xffffffffu, lab[t] > 0.0f);
+                un |= bt;
+                if (lane == 0 && t < a.B) a.tok_bits[(int64_t)t * a.W + w] = bt;
             }
+            if (lane == 0) a.seg_bits[w] = un;
+        }
+        __syncthreads();
+        if (tid == 0) grid_wait(a.grid_bar, grid_arrive(a.grid_bar), ctl, a.err);
+        __syncthreads();
+        for (int w = tid; w < a.W; w += kSfThreads) {
+            ubits[w] = __ldcg(a.seg_bits + w);
+#pragma unroll
+            for (int t = 0; t < NT; ++t)
+                if (t < a.B) tbits[t * a.W + w] = __ldcg(a.tok_bits + (int64_t)t * a.W + w);
         }
     }
     __syncthreads();
@@ -859,7 +662,7 @@ __global__ void __launch_bounds__(kSfThreads, 1) stream_ffn_kernel(const SfArgs 
 
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
-template <int NT, int WT, int CPT, bool kPred = false>
+template <int NT, int WT, int CPT>
 int launch_sf(const StreamFfnArgs &fa, cudaStream_t st) {
     SfArgs a{};
     const int64_t rb = row_bytes_of<WT>(fa.d);
@@ -908,26 +711,9 @@ int launch_sf(const StreamFfnArgs &fa, cudaStream_t st) {
     a.off_bits = a.off_stage;
     const size_t need_bits = a.off_stage + sizeof(uint32_t) * (size_t)a.W * (1 + NT);
     if (need_bits > smem) smem = need_bits;
-    if (kPred) {
-        // the predictor's region in the ring, after the union words
-        a.p1 = fa.p1;
-        a.p2 = fa.p2;
-        a.hidden = fa.hidden;
-        a.logits = fa.logits;
-        a.hist = fa.hist;
-        a.bits_out = fa.bits_out;
-        a.D = fa.D;
-        a.k = fa.k;
-        a.prows = (fa.f + grid - 1) / grid;
-        a.off_pred = (int)align_up(need_bits, 128);
-        const size_t pred = sizeof(__half) * (size_t)(fa.d + fa.D) +
-                            sizeof(uint32_t) * ((size_t)((a.prows + 3) & ~3) + kHistBins) +
-                            std::max(sizeof(__half) * (size_t)a.prows * fa.D, (sizeof(uint2) + sizeof(float)) * (size_t)fa.f);
-        if (a.off_pred + pred > smem) smem = a.off_pred + pred;
-    }
     if (smem > kSfSmemLimit) return fail(SPB_ERR_UNSUPPORTED, "stream ffn: shared memory");
     a.trace = static_cast<unsigned long long *>(trace_buffer((size_t)grid * kSfTraceSlots));
-    auto kern = stream_ffn_kernel<NT, WT, CPT, kPred>;
+    auto kern = stream_ffn_kernel<NT, WT, CPT>;
     if (int rc = ensure_smem((const void *)kern, smem)) return rc;
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(grid);
@@ -952,14 +738,6 @@ int launch_sf(const StreamFfnArgs &fa, cudaStream_t st) {
 template <int WT>
 int launch_sf_wt(const StreamFfnArgs &fa, cudaStream_t st) {
     const int cpt = (fa.d / 8 + kSfConsumers - 1) / kSfConsumers;
-    if constexpr (WT == SPB_W_F16) {
-        if (fa.p1) {
-            if (fa.B != 1) return fail(SPB_ERR_UNSUPPORTED, "stream ffn: the fused predictor serves one token");
-            return cpt == 1 ? launch_sf<1, WT, 1, true>(fa, st) : launch_sf<1, WT, 2, true>(fa, st);
-        }
-    } else {
-        if (fa.p1) return fail(SPB_ERR_UNSUPPORTED, "stream ffn: the fused predictor serves fp16 weights");
-    }
     if (cpt == 1) {
         if (fa.B <= 1) return launch_sf<1, WT, 1>(fa, st);
         if (fa.B <= 2) return launch_sf<2, WT, 1>(fa, st);
