@@ -25,7 +25,8 @@ partial outputs per layer: NCCL's, or with --peer the library's one-shot
 kernel over NVLink peer memory): strong scaling of the same layer, so N = 1 is
 the single-GPU run.  --replicas runs independent copies instead.
 
-The JSON line adds: per_batch (the same layer at B = 1..32), dense_cublas
+The JSON line adds: e2e_bits (e2e with the sets as bit words instead of
+fp32 labels), per_batch (the same layer at B = 1..32), dense_cublas
 (the dense FFN through cuBLAS fp16 GEMMs with fp32 accumulation, same
 config), device_error (the workspace's error word after every timed region;
 non-zero fails the run), shard_parity / allreduce_us (the step's collective
@@ -463,6 +464,35 @@ def run_ours(a):
     ms_e2e, _ = etimer.time(K, max(3, head["reps"] // 2), dist, device)
     errors.append(spb.device_error(ws))
 
+    # the same end to end with the sets as bit words (spb_ffn_forward_bits:
+    # 1/32 of the label bytes cross PCIe), single GPU without the predictor
+    e2e_bits = None
+    if not a.predictor and not sharded:
+        W = (f + 31) // 32
+
+        def words(lab):
+            b = np.packbits(lab > 0, axis=1, bitorder="little")
+            b = np.pad(b, ((0, 0), (0, 4 * W - b.shape[1])))
+            return torch.from_numpy(np.ascontiguousarray(b).view(np.int32)).pin_memory()
+
+        pbits = [words(ly["lab_np"]) for ly in layers]
+        bitsin = [torch.empty((a.batch, W), dtype=torch.int32, device=device) for _ in layers]
+
+        def e2e_bits_body(i):
+            xin[i].copy_(pinned[i]["x"], non_blocking=True)
+            bitsin[i].copy_(pbits[i], non_blocking=True)
+            spb.ffn_forward(*Wl[i], xin[i], bits=bitsin[i], f=f, wtype=wtype, out=layers[i]["out"],
+                            per_token_mask=bool(a.per_token), path=path, workspace=ws)
+            pinned[i]["out"].copy_(layers[i]["out"], non_blocking=True)
+
+        btimer = Timer(torch, stream, L, e2e_bits_body, graphs=True)
+        btimer.warm(3)
+        ms_b, _ = btimer.time(K, max(3, head["reps"] // 2), dist, device)
+        errors.append(spb.device_error(ws))
+        e2e_bits = {"value": tokens_per_step / (ms_b / 1e3), "unit": "tokens/s", "ms_per_step": ms_b,
+                    "h2d_bytes_per_step": a.batch * d * 4 + a.batch * W * 4, "d2h_bytes_per_step": a.batch * d * 4,
+                    "sets": "bit words [B][ceil(f/32)] (spb_ffn_forward_bits)"}
+
     rec = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": ws_n, "steps": K, "warmup": a.warmup,
         "ms_per_step": ms, "higher_is_better": True, "scaling": "strong" if sharded else "weak",
@@ -477,6 +507,7 @@ def run_ours(a):
         "e2e": {"value": tokens_per_step / (ms_e2e / 1e3), "unit": "tokens/s",
                 "h2d_bytes_per_step": a.batch * d * 4 + (0 if a.predictor else a.batch * (f1 - f0) * 4),
                 "d2h_bytes_per_step": a.batch * d * 4, "ms_per_step": ms_e2e},
+        "e2e_bits": e2e_bits,
         "clocks": head["clocks"],
         "timing": {"repeats": head["reps"], "ms_per_step_samples": [round(s, 5) for s in head["samples"]],
                    "statistic": "median over repeats of the K-step region"},
