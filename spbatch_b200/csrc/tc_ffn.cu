@@ -69,7 +69,7 @@ constexpr int kTcWarps = kTcThreads / 32;
 constexpr int kTileM = 128;          // neurons per gate/up tile (MMA M)
 constexpr int kDnRows = 64;          // union positions per down stage
 constexpr int kBoxRows = 32;         // rows per weight TMA box when whole row ranges stream
-constexpr int kDenseMinPermille = 960;  // union share of f from which whole row ranges stream
+constexpr int kDenseMinPermille = 900;  // union share of f from which whole row ranges may stream
 constexpr int kSlice = 256;          // output columns per down unit (two M = 128 MMAs)
 constexpr uint32_t kATile = 16384;   // 128 rows x 128 bytes (one 64-wide K block)
 constexpr uint32_t kDnLbo = (kDnRows / 8) * 1024;  // byte distance between 64-column blocks of a down stage
@@ -682,7 +682,13 @@ ffn_tc_kernel(const __grid_constant__ TcMaps maps, const TcArgs a) {
     // A union covering most of the neurons streams whole row ranges: every
     // neuron is a position (Uv = f), rows arrive as 2-D TMA boxes at the
     // copy engine's rate, and the inactive neurons' h is zero by the mask.
-    const bool dense = !kQuant && U >= a.dense_min;
+    // ...when it also needs no more tiles per cluster than the gathered union
+    // (the row-range shares are whole kBoxRows boxes): at 7B B = 32 (U/f =
+    // 0.85) the gather fits one 128-row tile per cluster and whole ranges
+    // two (87 against 69 us); at 13B B = 64 (U/f = 0.93) both need two and
+    // whole ranges win (112.6 against 122.7 us).
+    const bool dense = !kQuant && U >= a.dense_min &&
+                       tiles_of(kBoxRows * ((a.W * 32 / kBoxRows + nclu - 1) / nclu)) <= tiles_of((U + nclu - 1) / nclu);
     const int Uv = dense ? a.f : U;
     // gate/up work of this cluster
     const int P0 = span_start(dense, Uv, clu, nclu);
