@@ -173,6 +173,12 @@ int spb_dequantize_rows(const void *q, int wtype, int rows, int d, float *out, v
  *   idx_out    [B][k > 0 ? k : f] (nullable): ascending active ids per token
  *   count_out  [B] (nullable), logits_out [B][f] (nullable)
  * d and D must be multiples of 256; workspace: spb_predict_workspace_bytes.
+ * One token with k > 0 and no idx_out is one cooperative launch of one CTA
+ * per SM (P2 slices resident in shared memory, the exact top-k in the same
+ * launch).  Its two grid barriers count on a counter the library keeps in
+ * each device's memory.  Full-device cooperative launches do not overlap, so
+ * calls on several streams of one device are serialised by the GPU.  If a
+ * barrier wait ever ran out (2 s), count_out[0] is -1.
  */
 size_t spb_predict_workspace_bytes(int B, int D, int f);
 int spb_predict(const void *p1, const void *p2, const float *x, int B, int d, int D, int f, int k, float threshold,

@@ -66,6 +66,31 @@ def test_invalid_arguments_fail_without_device(spb):
     assert rc == 1
 
 
+def test_peer_allreduce_rejects_bad_arguments_without_device(spb):
+    """spb_allreduce_peer validates everything before it launches."""
+    L = spb.lib()
+    assert L.spb_peer_handle_bytes() >= 64  # a CUDA IPC handle plus the pointer's offset
+    assert L.spb_peer_sync_bytes() >= 4 * (16 + 8)
+    fake = C.c_void_p(256)
+    ptrs = (C.c_void_p * 2)(256, 512)
+    err = C.c_void_p(1024)
+    rc = L.spb_allreduce_peer(None, ptrs, ptrs, 2, 0, 1024, fake, 1024, err, None)
+    assert rc == 1 and b"null" in L.spb_last_error()
+    rc = L.spb_allreduce_peer(fake, ptrs, ptrs, 9, 0, 1024, fake, 1024, err, None)
+    assert rc == 1 and b"world" in L.spb_last_error()
+    rc = L.spb_allreduce_peer(fake, ptrs, ptrs, 2, 2, 1024, fake, 1024, err, None)
+    assert rc == 1 and b"rank" in L.spb_last_error()
+    rc = L.spb_allreduce_peer(fake, ptrs, ptrs, 2, 0, 1024, fake, 1022, err, None)
+    assert rc == 1 and b"multiples of 4" in L.spb_last_error()
+    rc = L.spb_allreduce_peer(fake, ptrs, ptrs, 2, 0, 512, fake, 1024, err, None)
+    assert rc == 1 and b"n <= stride" in L.spb_last_error()
+    unaligned = (C.c_void_p * 2)(256, 520)
+    rc = L.spb_allreduce_peer(fake, unaligned, ptrs, 2, 0, 1024, fake, 1024, err, None)
+    assert rc == 1 and b"aligned" in L.spb_last_error()
+    rc = L.spb_peer_export(None, None)
+    assert rc == 1
+
+
 def test_python_wrappers_refuse_cpu_tensors(spb):
     import torch
     x = torch.zeros(2, 64)
