@@ -187,6 +187,21 @@ def layer_copies(a, bytes_per_layer):
     return a.layers or int(min(32, max(4, math.ceil(3 * L2_BYTES / bytes_per_layer))))
 
 
+def rotation(a, d, f, ws_n, sharded):
+    """Whether the per-batch curve runs, and the layer copies rotated: enough
+    for the smallest batch timed (both arms use it, so their records match)."""
+    from spbatch_b200.workload import active_bytes
+    w_bytes = {"f16": 2.0, "q8_0": 34 / 32, "q4_0": 18 / 32}[a.wtype]
+    pred_bytes = (d * PRED_RANK + PRED_RANK * (f // (ws_n if sharded else 1))) * 2 if a.predictor else 0
+    sweep = (not a.no_sweep and ws_n == 1 and a.wtype == "f16" and not a.predictor and a.model == "7b"
+             and a.batch == 32)
+    Bs = sorted(set(SWEEP_BATCHES) | {a.batch}) if sweep else [a.batch]
+    est_min = min(active_bytes(d, min(f, int(a.activity * f * min(B, 8))), B, w_bytes, pred_bytes) for B in Bs)
+    if sharded:
+        est_min /= ws_n
+    return sweep, layer_copies(a, est_min)
+
+
 def make_weights(a, L, d, f0, f1, device, seed):
     """L weight copies [f1 - f0][d] (this rank's rows) in the requested format."""
     import torch
@@ -309,15 +324,7 @@ def run_ours(a):
     pred_bytes = (d * PRED_RANK + PRED_RANK * (f1 - f0)) * 2 if a.predictor else 0
 
     # layer copies: enough for the smallest batch the run times
-    Bs = [a.batch]
-    sweep = (not a.no_sweep and ws_n == 1 and a.wtype == "f16" and not a.predictor and a.model == "7b"
-             and a.batch == 32)
-    if sweep:
-        Bs = sorted(set(SWEEP_BATCHES) | {a.batch})
-    est_min = min(active_bytes(d, min(f, int(a.activity * f * min(B, 8))), B, w_bytes, pred_bytes) for B in Bs)
-    if sharded:
-        est_min /= ws_n
-    L = layer_copies(a, est_min)
+    sweep, L = rotation(a, d, f, ws_n, sharded)
     Wl = make_weights(a, L, d, f0, f1, device, 1234 + (0 if sharded else rank))
     P = None
     pws = None
@@ -647,8 +654,7 @@ def run_reference(a):
     from spbatch_b200.workload import SHAPES, active_bytes, zipf_active_labels
     d, f = SHAPES[a.model]["d"], SHAPES[a.model]["f"]
     k = int(round(a.activity * f))
-    est = active_bytes(d, min(f, int(a.activity * f * min(a.batch, 8))), a.batch, 2.0)
-    L = layer_copies(a, est)
+    _, L = rotation(a, d, f, ws_n, ws_n > 1 and not a.replicas)
     g = torch.Generator().manual_seed(1234)
     # one fp16-valued weight set: the dense CPU path's cost does not depend on the values
     W = [(torch.randn((f, d), generator=g) * 0.02).half().float().numpy() for _ in range(3)]
