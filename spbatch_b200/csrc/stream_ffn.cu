@@ -643,12 +643,22 @@ __global__ void __launch_bounds__(kSfThreads, 1) stream_ffn_kernel(const SfArgs 
             for (int k = 0; k < CPT; ++k) {
                 const int c = tid + k * kSfConsumers;
                 if (c >= d8) continue;
+                // Every CTA adds into the same [B][d] addresses at about the
+                // same time: CTA b starts at token b mod NT, so concurrent
+                // CTAs spread over the tokens' rows (one static order per
+                // rotation, so the registers stay statically indexed).
+                const int rot = (int)(blockIdx.x & (NT - 1));
 #pragma unroll
-                for (int t = 0; t < NT; ++t) {
-                    if (t < a.B) {
-                        float4 *o = reinterpret_cast<float4 *>(a.out + (int64_t)t * a.d + c * 8);
-                        atomicAdd(o, make_float4(acc[k][t][0], acc[k][t][1], acc[k][t][2], acc[k][t][3]));
-                        atomicAdd(o + 1, make_float4(acc[k][t][4], acc[k][t][5], acc[k][t][6], acc[k][t][7]));
+                for (int r = 0; r < NT; ++r) {
+                    if (rot != r) continue;
+#pragma unroll
+                    for (int q = 0; q < NT; ++q) {
+                        const int t = (q + r) % NT;
+                        if (t < a.B) {
+                            float4 *o = reinterpret_cast<float4 *>(a.out + (int64_t)t * a.d + c * 8);
+                            atomicAdd(o, make_float4(acc[k][t][0], acc[k][t][1], acc[k][t][2], acc[k][t][3]));
+                            atomicAdd(o + 1, make_float4(acc[k][t][4], acc[k][t][5], acc[k][t][6], acc[k][t][7]));
+                        }
                     }
                 }
             }
